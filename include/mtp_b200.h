@@ -1,0 +1,203 @@
+/*
+ * mtp_b200.h -- C ABI of the B200-native (sm_100a) tree-verification hot path.
+ *
+ * Every entry point replaces one operator of Dahacker444/mtp-engine's Python
+ * API (the citation beside each declaration is the reference function it
+ * replaces, file:line within that project).  Conventions:
+ *
+ *   - plain device pointers, element counts and dtype codes; no torch types;
+ *   - every tensor is dense and row-major (the reference's wrappers call
+ *     .contiguous() before launching, e.g. mtp_kernels.py:945-946);
+ *   - outputs and workspaces are allocated by the caller (the reference
+ *     allocates outputs with torch.empty, mtp_kernels.py:960); the library
+ *     never calls cudaMalloc, so calls are safe inside CUDA-graph capture;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default);
+ *     nothing synchronises the host except mtp_device_status();
+ *   - the return value is an MTP_* status; mtp_last_error() gives a
+ *     thread-local message for the last non-zero status.
+ *
+ * Device-side checks (page ids out of range, inconsistent page tables,
+ * bounded waits that ran out) are recorded in a per-device error word that
+ * mtp_device_status() reads.
+ */
+#ifndef MTP_B200_H
+#define MTP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define MTP_DTYPE_F32 0
+#define MTP_DTYPE_BF16 1
+#define MTP_DTYPE_F16 2
+#define MTP_DTYPE_E4M3 3 /* float8_e4m3fn */
+
+/* status codes */
+#define MTP_OK 0
+#define MTP_ERR_SHAPE 1       /* inconsistent or unsupported sizes */
+#define MTP_ERR_DTYPE 2       /* dtype combination not supported */
+#define MTP_ERR_ALIGN 3       /* pointer alignment violated */
+#define MTP_ERR_CUDA 4        /* a CUDA runtime call failed */
+#define MTP_ERR_TIMEOUT 5     /* a bounded device wait ran out */
+#define MTP_ERR_WORKSPACE 6   /* workspace missing or too small */
+#define MTP_ERR_DEVICE 7      /* a device-side check failed */
+#define MTP_ERR_ARG 8         /* null pointer or bad scalar argument */
+
+/* ABI version of this header (bumped on any signature change). */
+int mtp_abi_version(void);
+
+/* Thread-local description of the last failing call on this thread. */
+const char* mtp_last_error(void);
+
+/* Synchronises `stream`, then reports the current device's error word
+ * (0 = clean, else an MTP_ERR_* code recorded by a kernel) in *code_out.
+ * clear != 0 resets the word.  Returns MTP_OK or MTP_ERR_CUDA. */
+int mtp_device_status(void* stream, int* code_out, int clear);
+
+/* ------------------------------------------------------------------------- */
+/* RMSNorm -> linear                                                          */
+/* ------------------------------------------------------------------------- */
+
+/* Bytes of workspace mtp_rmsnorm_linear needs for these sizes. */
+size_t mtp_rmsnorm_linear_workspace(int64_t M, int64_t K, int has_norm_weight);
+
+/* y[M,N] = ((rmsnorm(x) * norm_weight) @ W^T + bias) * scale.
+ * Replaces fused_rmsnorm_linear, mtp_kernels.py:936-977 (eager reference
+ * _eager_rmsnorm_linear, mtp_kernels.py:778-787).  norm_weight (the RMSNorm
+ * gamma, [K]) may be NULL, which is the reference's signature; bias may be
+ * NULL.  x/W/y dtypes: bf16 or f16 with x, W and y all equal runs on the
+ * tcgen05 tensor cores (fp32 accumulation); any mix involving f32 runs the
+ * fp32 CUDA-core kernel (IEEE fp32 throughout, like the reference). */
+int mtp_rmsnorm_linear(const void* x, int x_dtype, const void* weight, int w_dtype,
+                       const void* bias, int bias_dtype, const void* norm_weight, int norm_dtype,
+                       void* y, int y_dtype, int64_t M, int64_t N, int64_t K, float eps,
+                       float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace mtp_rmsnorm_linear_fp8 needs for these sizes. */
+size_t mtp_rmsnorm_linear_fp8_workspace(int64_t M, int64_t K);
+
+/* y[M,N] = rmsnorm(x) @ (W * wscale[:,None])^T + bias.
+ * Replaces fused_rmsnorm_linear_fp8, mtp_kernels.py:1014-1044 (eager
+ * reference _eager_rmsnorm_linear_fp8, mtp_kernels.py:804-814).  wscale is
+ * the fp32 per-output-channel scale, typically a slice of the flat buffer
+ * of pack_scales (mtp_kernels.py:1336-1353), i.e. flat + offsets[idx].
+ * With an E4M3 weight the activations are quantised per token
+ * (sx = amax_row / 448) and the product runs on the tensor cores
+ * (kind::f8f6f4); rstd is computed from the dequantised activations, so the
+ * result equals the reference evaluated on those dequantised activations.
+ * x may also be passed pre-quantised (x_dtype = E4M3, x_scale = sx[M]).
+ * A non-E4M3 weight (the reference's own fp32-valued self-check weight,
+ * mtp_engine.py:1792-1800) runs unquantised in fp32. */
+int mtp_rmsnorm_linear_fp8(const void* x, int x_dtype, const float* x_scale,
+                           const void* weight, int w_dtype, const float* wscale,
+                           const void* bias, int bias_dtype, void* y, int y_dtype,
+                           int64_t M, int64_t N, int64_t K, float eps,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* attention                                                                  */
+/* ------------------------------------------------------------------------- */
+
+/* out[B,H,D] = softmax(q k^T * scale, keys with mask[j] <= 0.5 dropped) v.
+ * Replaces fused_tree_attention, mtp_kernels.py:1165-1191 (eager
+ * _eager_tree_attention, 859-872).  k, v: [B,H,L,D]; mask: [L] float32
+ * shared by every (b,h).  dtype applies to q, k, v and out. */
+int mtp_tree_attention(const void* q, const void* k, const void* v, const float* mask, void* out,
+                       int dtype, int64_t B, int64_t H, int64_t L, int64_t D, float scale,
+                       void* stream);
+
+/* Single-query attention over a page pool with a per-token page table.
+ * Replaces fused_paged_attention, mtp_kernels.py:1136-1162 (eager
+ * _eager_paged_attention, 832-856).  k_pages/v_pages:
+ * [num_pages, B, H, page_size, D] (PagedKVCache layout, mtp_engine.py:542-549);
+ * page_table: [B, L] int32, token t of sequence b at
+ * pages[page_table[b,t], b, h, t % page_size]. */
+int mtp_paged_attention(const void* q, const void* k_pages, const void* v_pages,
+                        const int32_t* page_table, void* out, int dtype, int64_t B, int64_t H,
+                        int64_t L, int64_t D, int64_t num_pages, int64_t page_size, float scale,
+                        void* stream);
+
+/* Bytes of workspace mtp_tree_attention_paged needs. */
+size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv,
+                                          int64_t D, int64_t ctx_len);
+
+/* Paged tree attention with GQA (the composite of fused_paged_attention and
+ * fused_tree_attention, mtp_kernels.py:1136-1191; it has no single
+ * counterpart in the reference).  For tree node n and query head h
+ * (kv head h / (Hq/Hkv)) the keys are the ctx_len context tokens of
+ * sequence b (paged, as in mtp_paged_attention; page_table row stride
+ * `table_stride` >= ctx_len) followed by the tree nodes m with
+ * tree_mask[n,m] > 0.5 (SpeculativeDraftTree.tree_mask,
+ * mtp_engine.py:671-680).  q/out: [B,T,Hq,D]; tree_k/tree_v: [B,Hkv,T,D];
+ * tree_mask: [T,T] float32. */
+int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_pages,
+                             const int32_t* page_table, int64_t table_stride, int64_t ctx_len,
+                             const void* tree_k, const void* tree_v, const float* tree_mask,
+                             void* out, int dtype, int64_t B, int64_t T, int64_t Hq, int64_t Hkv,
+                             int64_t D, int64_t num_pages, int64_t page_size, float scale,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* verification (lm_head GEMM -> argmax -> acceptance)                        */
+/* ------------------------------------------------------------------------- */
+
+/* Bytes of verify workspace for `rows` (= B*S or M) logit rows. */
+size_t mtp_verify_workspace(int64_t rows);
+
+/* Puts a verify workspace into its resting state.  Needed once after
+ * allocation; every verify call leaves the workspace in that state again. */
+int mtp_verify_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* top[m] = argmax_v(hidden[m] . W[v] + bias[v]); accept[m] = top[m] == draft[m].
+ * Replaces fused_verify, mtp_fused_verify.py:199-234 (eager
+ * _eager_fused_verify, 159-166).  accept: int8 [M], top: int32 [M],
+ * draft: int32 [M].  No logits are written to memory. */
+int mtp_fused_verify(const void* hidden, int h_dtype, const void* weight, int w_dtype,
+                     const void* bias, int bias_dtype, const int32_t* draft, int8_t* accept,
+                     int32_t* top, int64_t M, int64_t K, int64_t V, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* Chain verification.  Replaces fused_multi_verify,
+ * mtp_fused_verify.py:237-290 (eager _eager_fused_multi_verify, 169-196).
+ * hidden: [B,S,K]; weight: [V,K]; draft: int32 [B,S-1]; accept: int8 [B,S-1]
+ * (prefix-gated: 1 only while every earlier draft matched);
+ * accepted_n: int32 [B]; corrected: int32 [B] (argmax at position 0). */
+int mtp_fused_multi_verify(const void* hidden, int h_dtype, const void* weight, int w_dtype,
+                           const void* bias, int bias_dtype, const int32_t* draft, int8_t* accept,
+                           int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S,
+                           int64_t K, int64_t V, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Vocab-parallel verify, step 1 (per rank): fold this rank's vocabulary
+ * block [vocab_offset, vocab_offset + V_shard) into keys[M] (int64, in place,
+ * keys must start at INT64_MIN or hold earlier partial maxima).
+ * key = (signed-ordered fp32 logit << 32) | (0xFFFFFFFF - global index), so
+ * max over keys = argmax with ties to the lowest index.  Step 2 is an
+ * all-reduce(MAX) of keys over the ranks (int64).  This pair replaces the
+ * gathered logits of RowParallelLinear, mtp_parallel.py:84-118. */
+int mtp_verify_shard_keys(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                          const void* bias_shard, int bias_dtype, int64_t* keys, int64_t M,
+                          int64_t K, int64_t V_shard, int64_t vocab_offset, void* stream);
+
+/* Vocab-parallel verify, step 3: decode reduced keys [B*S] into the outputs
+ * of mtp_fused_multi_verify and reset keys to INT64_MIN. */
+int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* accept,
+                               int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S,
+                               void* stream);
+
+/* Fills keys[n] with INT64_MIN. */
+int mtp_keys_fill(int64_t* keys, int64_t n, void* stream);
+
+/* Number of kernels this library has launched in this process (all
+ * devices).  Benchmarks read it around a timed region. */
+uint64_t mtp_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MTP_B200_H */

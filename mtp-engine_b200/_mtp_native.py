@@ -1,0 +1,175 @@
+"""ctypes binding of libmtp_b200.so (include/mtp_b200.h) plus the host-side
+plumbing shared by the drop-in modules: dtype codes, stream handles, cached
+per-(device, stream) workspaces and status -> exception mapping.
+
+There is no fallback: if the library is missing or a tensor is not on a CUDA
+device, the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Dict, Optional, Tuple
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmtp_b200.so")
+
+DT_F32, DT_BF16, DT_F16, DT_E4M3 = 0, 1, 2, 3
+_DTYPE_CODES = {torch.float32: DT_F32, torch.bfloat16: DT_BF16, torch.float16: DT_F16}
+if hasattr(torch, "float8_e4m3fn"):
+    _DTYPE_CODES[torch.float8_e4m3fn] = DT_E4M3
+
+STATUS_NAMES = {0: "OK", 1: "MTP_ERR_SHAPE", 2: "MTP_ERR_DTYPE", 3: "MTP_ERR_ALIGN", 4: "MTP_ERR_CUDA",
+                5: "MTP_ERR_TIMEOUT", 6: "MTP_ERR_WORKSPACE", 7: "MTP_ERR_DEVICE", 8: "MTP_ERR_ARG"}
+
+_vp, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/mtp_b200.h
+SIGNATURES = {
+    "mtp_abi_version": (_i, []),
+    "mtp_last_error": (ctypes.c_char_p, []),
+    "mtp_device_status": (_i, [_vp, ctypes.POINTER(_i), _i]),
+    "mtp_rmsnorm_linear_workspace": (_sz, [_i64, _i64, _i]),
+    "mtp_rmsnorm_linear": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _vp, _i, _i64, _i64, _i64, _f, _f,
+                                _vp, _sz, _vp]),
+    "mtp_rmsnorm_linear_fp8_workspace": (_sz, [_i64, _i64]),
+    "mtp_rmsnorm_linear_fp8": (_i, [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _vp, _i, _i64, _i64, _i64, _f,
+                                    _vp, _sz, _vp]),
+    "mtp_tree_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _f, _vp]),
+    "mtp_paged_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _f, _vp]),
+    "mtp_tree_attention_paged_workspace": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64]),
+    "mtp_tree_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64,
+                                      _i64, _i64, _i64, _i64, _f, _vp, _sz, _vp]),
+    "mtp_verify_workspace": (_sz, [_i64]),
+    "mtp_verify_workspace_init": (_i, [_vp, _sz, _vp]),
+    "mtp_fused_verify": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "mtp_fused_multi_verify": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                    _vp, _sz, _vp]),
+    "mtp_verify_shard_keys": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
+    "mtp_launch_count": (ctypes.c_uint64, []),
+}
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load libmtp_b200.so (once).  Raises if it was not built."""
+    global _lib
+    if _lib is None:
+        with _lib_lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python mtp-engine_b200/_build.py` "
+                        "(this package has no CPU or Triton fallback)")
+                L = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = L
+    return _lib
+
+
+class MTPError(RuntimeError):
+    pass
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = lib().mtp_last_error().decode(errors="replace")
+        raise MTPError(f"{what} failed with {STATUS_NAMES.get(status, status)}: {msg}")
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("mtp-engine-b200 operators run on CUDA tensors only "
+                             f"(got a tensor on {t.device}); there is no CPU fallback")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
+    if dev is None:
+        raise ValueError("no tensor given")
+    return dev
+
+
+def stream_handle(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+# --------------------------------------------------------------------------- #
+# workspaces: one set per (device, stream); calls on one stream are ordered,
+# so reusing the buffer across calls on that stream is race-free.
+# --------------------------------------------------------------------------- #
+_ws: Dict[Tuple[int, int, str], torch.Tensor] = {}
+_ws_lock = threading.Lock()
+
+
+def workspace(device: torch.device, name: str, nbytes: int, init=None) -> torch.Tensor:
+    """Cached uint8 device buffer of at least `nbytes`.  `init(buf)` runs
+    (on the current stream) whenever a new buffer is allocated."""
+    nbytes = max(int(nbytes), 256)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream, name)
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            if init is not None:
+                init(buf)
+            _ws[key] = buf
+    return buf
+
+
+def drop_workspace(device: torch.device, name: str) -> None:
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream, name)
+    with _ws_lock:
+        _ws.pop(key, None)
+
+
+def verify_workspace(device: torch.device, rows: int) -> torch.Tensor:
+    """Keys + ticket counter for the fused verify kernels.  Initialised once;
+    every verify call leaves it initialised again."""
+    need = lib().mtp_verify_workspace(int(rows))
+
+    def _init(buf):
+        check(lib().mtp_verify_workspace_init(ptr(buf), buf.numel(), stream_handle(device)),
+              "mtp_verify_workspace_init")
+
+    return workspace(device, "verify", need, _init)
+
+
+def device_status(device: torch.device, clear: bool = True) -> int:
+    code = ctypes.c_int(0)
+    with torch.cuda.device(device):
+        check(lib().mtp_device_status(stream_handle(device), ctypes.byref(code), int(clear)),
+              "mtp_device_status")
+    return code.value
+
+
+def exported_symbols():
+    return list(SIGNATURES)

@@ -1,0 +1,546 @@
+// mtp_abi.cu -- the C ABI (include/mtp_b200.h): argument checks, workspace
+// carving, kernel selection and launches.  Built as one translation unit so
+// every kernel shares the per-device error word.
+//
+// Nothing here allocates device memory or synchronises the host (except
+// mtp_device_status), so every entry point can be captured in a CUDA graph
+// and called on any stream.
+
+#include <atomic>
+#include <mutex>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "mtp_attention.cuh"
+#include "mtp_gemm_simt.cuh"
+#include "mtp_gemm_tc.cuh"
+#include "mtp_rownorm.cuh"
+#include "mtp_verify.cuh"
+
+using namespace mtp;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+constexpr int kMaxDevices = 64;
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define MTP_CUDA_TRY(expr)                                                                  \
+  do {                                                                                      \
+    cudaError_t e_ = (expr);                                                                \
+    if (e_ != cudaSuccess) return fail(MTP_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+std::atomic<uint64_t> g_launches{0};
+
+// after every kernel launch: surface launch errors, count the launch
+#define MTP_LAUNCH_CHECK()                  \
+  do {                                      \
+    MTP_CUDA_TRY(cudaGetLastError());       \
+    g_launches.fetch_add(1, std::memory_order_relaxed); \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+inline bool is16bit(int dt) { return dt == MTP_DTYPE_BF16 || dt == MTP_DTYPE_F16; }
+inline bool valid_dtype(int dt) { return dt >= MTP_DTYPE_F32 && dt <= MTP_DTYPE_E4M3; }
+
+int current_device(int* dev) {
+  MTP_CUDA_TRY(cudaGetDevice(dev));
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(MTP_ERR_CUDA, "device index %d out of range", *dev);
+  return MTP_OK;
+}
+
+int sm_count(int dev) {
+  static int cache[kMaxDevices] = {0};
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// ---------------------------------------------------------------- tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major operand [rows, cols] with a row pitch of `row_bytes`, loaded in
+// boxes of (128 bytes of K) x box_rows with the 128-byte swizzle.
+int make_kmajor_map(CUtensorMap* map, const void* base, bool fp8, int dt16, int64_t rows, int64_t cols,
+                    int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(MTP_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int eb = fp8 ? 1 : 2;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(cols * eb)};
+  const cuuint32_t box[2] = {(cuuint32_t)(128 / eb), (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType t = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                    : (dt16 == MTP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  CUresult r = enc(map, t, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTP_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MTP_OK;
+}
+
+// ---------------------------------------------------------------- GEMM launchers
+template <int BN, bool FP8, int FMT>
+int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int num_kb, const GemmEpilogue& ep,
+                   cudaStream_t s) {
+  auto kern = tc::gemm_tc_kernel<BN, FP8, FMT>;
+  constexpr int smem = tc::Cfg<BN>::SMEM_BYTES;
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  static bool attr_done[kMaxDevices] = {false};
+  if (!attr_done[dev]) {
+    MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done[dev] = true;
+  }
+  const int tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + BN - 1) / BN);
+  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+  kern<<<grid, tc::kThreads, smem, s>>>(ta, tb, M, N, num_kb, ep);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+// A [M,K] and B [N,K] both K-major, 16-bit (ab_dtype) or E4M3 (fp8).
+int launch_gemm_tc(const void* A, const void* B, int ab_dtype, bool fp8, int64_t M, int64_t N, int64_t K,
+                   const GemmEpilogue& ep, cudaStream_t s) {
+  const int bn = N > 128 ? 256 : 128;
+  CUtensorMap ta, tb;
+  if (int st = make_kmajor_map(&ta, A, fp8, ab_dtype, M, K, tc::kBM)) return st;
+  if (int st = make_kmajor_map(&tb, B, fp8, ab_dtype, N, K, bn)) return st;
+  const int eb = fp8 ? 1 : 2;
+  const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  if (fp8) {
+    return bn == 256 ? launch_tc_inst<256, true, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s)
+                     : launch_tc_inst<128, true, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s);
+  }
+  if (ab_dtype == MTP_DTYPE_BF16)
+    return bn == 256 ? launch_tc_inst<256, false, 1>(ta, tb, (int)M, (int)N, num_kb, ep, s)
+                     : launch_tc_inst<128, false, 1>(ta, tb, (int)M, (int)N, num_kb, ep, s);
+  return bn == 256 ? launch_tc_inst<256, false, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s)
+                   : launch_tc_inst<128, false, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s);
+}
+
+bool tc_eligible(const void* A, const void* B, int a_dt, int b_dt, int64_t M, int64_t N, int64_t K) {
+  const bool fp8 = a_dt == MTP_DTYPE_E4M3 && b_dt == MTP_DTYPE_E4M3;
+  const bool h16 = is16bit(a_dt) && a_dt == b_dt;
+  if (!fp8 && !h16) return false;
+  const int eb = fp8 ? 1 : 2;
+  if ((K * eb) % 16 != 0) return false;  // TMA row pitch must be a multiple of 16 bytes
+  if (!aligned16(A) || !aligned16(B)) return false;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return false;
+  return true;
+}
+
+int launch_gemm_simt(const void* A, int a_dt, const void* B, int b_dt, int64_t M, int64_t N, int64_t K,
+                     const GemmEpilogue& ep, cudaStream_t s) {
+  if (M > 65535LL * simt::kTile) return fail(MTP_ERR_SHAPE, "M=%lld too large for the fp32 path", (long long)M);
+  dim3 grid((unsigned)((N + simt::kTile - 1) / simt::kTile), (unsigned)((M + simt::kTile - 1) / simt::kTile));
+  simt::gemm_simt_kernel<<<grid, 256, 0, s>>>(A, a_dt, B, b_dt, (int)M, (int)N, (int)K, ep);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+int launch_gemm(const void* A, int a_dt, const void* B, int b_dt, int64_t M, int64_t N, int64_t K,
+                const GemmEpilogue& ep, cudaStream_t s) {
+  if (tc_eligible(A, B, a_dt, b_dt, M, N, K))
+    return launch_gemm_tc(A, B, a_dt, a_dt == MTP_DTYPE_E4M3, M, N, K, ep, s);
+  return launch_gemm_simt(A, a_dt, B, b_dt, M, N, K, ep, s);
+}
+
+int launch_rownorm(const void* x, int x_dt, const void* gamma, int g_dt, const float* x_scale, int64_t M,
+                   int64_t K, float eps, int mode, float* row_out, void* xo, int xo_dt, cudaStream_t s) {
+  if (M == 0) return MTP_OK;
+  if (M > INT32_MAX) return fail(MTP_ERR_SHAPE, "too many rows");
+  rownorm_kernel<<<(unsigned)M, 256, 0, s>>>(x, x_dt, gamma, g_dt, x_scale, (int)K, eps, mode, row_out, xo, xo_dt);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+GemmEpilogue store_epilogue(const float* row_scale, const float* col_scale, const void* bias, int bias_dt,
+                            float scale, void* y, int y_dt, int64_t N) {
+  GemmEpilogue ep{};
+  ep.mode = EPI_STORE;
+  ep.row_scale = row_scale;
+  ep.col_scale = col_scale;
+  ep.bias = bias;
+  ep.bias_dtype = bias_dt;
+  ep.scale = scale;
+  ep.y = y;
+  ep.y_dtype = y_dt;
+  ep.ldy = N;
+  ep.y_vec_ok = is16bit(y_dt) && aligned16(y) && (N % 8 == 0);
+  return ep;
+}
+
+int check_dims(int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N < 0 || K < 0) return fail(MTP_ERR_SHAPE, "negative size");
+  if (K == 0) return fail(MTP_ERR_SHAPE, "K must be positive");
+  if (N > 0xFFFFFFFFLL || M > INT32_MAX || K > INT32_MAX) return fail(MTP_ERR_SHAPE, "size out of range");
+  return MTP_OK;
+}
+
+size_t verify_ws_bytes(int64_t rows) { return align256((size_t)rows * 8) + 256; }
+
+}  // namespace
+
+// =========================================================================
+extern "C" {
+
+int mtp_abi_version(void) { return kAbiVersion; }
+
+const char* mtp_last_error(void) { return g_err; }
+
+uint64_t mtp_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int mtp_device_status(void* stream, int* code_out, int clear) {
+  MTP_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
+  int code = 0;
+  MTP_CUDA_TRY(cudaMemcpyFromSymbol(&code, g_dev_error, sizeof(int)));
+  if (code_out) *code_out = code;
+  if (clear) {
+    const int zero = 0;
+    MTP_CUDA_TRY(cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int)));
+  }
+  return MTP_OK;
+}
+
+// ---------------------------------------------------------------- RMSNorm-linear
+size_t mtp_rmsnorm_linear_workspace(int64_t M, int64_t K, int has_norm_weight) {
+  return align256((size_t)M * 4) + (has_norm_weight ? align256((size_t)M * (size_t)K * 4) : 0);
+}
+
+int mtp_rmsnorm_linear(const void* x, int x_dtype, const void* weight, int w_dtype, const void* bias,
+                       int bias_dtype, const void* norm_weight, int norm_dtype, void* y, int y_dtype, int64_t M,
+                       int64_t N, int64_t K, float eps, float scale, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (int st = check_dims(M, N, K)) return st;
+  if (!valid_dtype(x_dtype) || !valid_dtype(w_dtype) || !valid_dtype(y_dtype) ||
+      x_dtype == MTP_DTYPE_E4M3 || y_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtype combination x=%d w=%d y=%d", x_dtype, w_dtype, y_dtype);
+  if (M == 0 || N == 0) return MTP_OK;
+  if (!x || !weight || !y) return fail(MTP_ERR_ARG, "null tensor pointer");
+  const size_t need = mtp_rmsnorm_linear_workspace(M, K, norm_weight != nullptr);
+  if (!workspace || workspace_bytes < need)
+    return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  cudaStream_t s = as_stream(stream);
+  float* rstd = static_cast<float*>(workspace);
+  const void* a = x;
+  if (norm_weight) {
+    void* xg = static_cast<uint8_t*>(workspace) + align256((size_t)M * 4);
+    if (int st = launch_rownorm(x, x_dtype, norm_weight, norm_dtype, nullptr, M, K, eps, ROW_GAMMA, rstd, xg,
+                                x_dtype, s))
+      return st;
+    a = xg;
+  } else {
+    if (int st = launch_rownorm(x, x_dtype, nullptr, 0, nullptr, M, K, eps, ROW_RSTD, rstd, nullptr, 0, s))
+      return st;
+  }
+  GemmEpilogue ep = store_epilogue(rstd, nullptr, bias, bias_dtype, scale, y, y_dtype, N);
+  const bool tc = x_dtype == w_dtype && x_dtype == y_dtype && tc_eligible(a, weight, x_dtype, w_dtype, M, N, K);
+  if (tc) return launch_gemm_tc(a, weight, x_dtype, false, M, N, K, ep, s);
+  return launch_gemm_simt(a, x_dtype, weight, w_dtype, M, N, K, ep, s);
+}
+
+size_t mtp_rmsnorm_linear_fp8_workspace(int64_t M, int64_t K) {
+  return align256((size_t)M * 4) + align256((size_t)M * (size_t)K);
+}
+
+int mtp_rmsnorm_linear_fp8(const void* x, int x_dtype, const float* x_scale, const void* weight, int w_dtype,
+                           const float* wscale, const void* bias, int bias_dtype, void* y, int y_dtype, int64_t M,
+                           int64_t N, int64_t K, float eps, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (int st = check_dims(M, N, K)) return st;
+  if (!valid_dtype(x_dtype) || !valid_dtype(w_dtype) || !valid_dtype(y_dtype) || y_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtype combination x=%d w=%d y=%d", x_dtype, w_dtype, y_dtype);
+  if (x_dtype == MTP_DTYPE_E4M3 && !x_scale)
+    return fail(MTP_ERR_ARG, "pre-quantised E4M3 activations need x_scale");
+  if (M == 0 || N == 0) return MTP_OK;
+  if (!x || !weight || !y || !wscale) return fail(MTP_ERR_ARG, "null tensor pointer");
+  const size_t need = mtp_rmsnorm_linear_fp8_workspace(M, K);
+  if (!workspace || workspace_bytes < need) return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  cudaStream_t s = as_stream(stream);
+  float* rowf = static_cast<float*>(workspace);
+  if (w_dtype != MTP_DTYPE_E4M3) {
+    // fp32-valued (or 16-bit) weight: the reference's unquantised semantics
+    if (x_dtype == MTP_DTYPE_E4M3) {
+      if (int st = launch_rownorm(x, x_dtype, nullptr, 0, x_scale, M, K, eps, ROW_PREQUANT, rowf, nullptr, 0, s))
+        return st;
+    } else if (int st = launch_rownorm(x, x_dtype, nullptr, 0, nullptr, M, K, eps, ROW_RSTD, rowf, nullptr, 0, s)) {
+      return st;
+    }
+    GemmEpilogue ep = store_epilogue(rowf, wscale, bias, bias_dtype, 1.0f, y, y_dtype, N);
+    return launch_gemm_simt(x, x_dtype, weight, w_dtype, M, N, K, ep, s);
+  }
+  const void* a = x;
+  if (x_dtype == MTP_DTYPE_E4M3) {
+    if (int st = launch_rownorm(x, x_dtype, nullptr, 0, x_scale, M, K, eps, ROW_PREQUANT, rowf, nullptr, 0, s))
+      return st;
+  } else {
+    void* xq = static_cast<uint8_t*>(workspace) + align256((size_t)M * 4);
+    if (int st = launch_rownorm(x, x_dtype, nullptr, 0, nullptr, M, K, eps, ROW_QUANT, rowf, xq, MTP_DTYPE_E4M3, s))
+      return st;
+    a = xq;
+  }
+  GemmEpilogue ep = store_epilogue(rowf, wscale, bias, bias_dtype, 1.0f, y, y_dtype, N);
+  return launch_gemm(a, MTP_DTYPE_E4M3, weight, MTP_DTYPE_E4M3, M, N, K, ep, s);
+}
+
+// ---------------------------------------------------------------- attention
+static int launch_decode_attention(const AttnArgs& a, cudaStream_t s) {
+  const int64_t rows = a.B * a.T * a.Hq;
+  if (rows == 0) return MTP_OK;
+  if (a.D > 32 * kAttnMaxDPerLane) return fail(MTP_ERR_SHAPE, "head_dim %lld > 256", (long long)a.D);
+  if (rows > INT32_MAX) return fail(MTP_ERR_SHAPE, "too many query rows");
+  decode_attention_kernel<<<(unsigned)rows, 128, 0, s>>>(a);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+int mtp_tree_attention(const void* q, const void* k, const void* v, const float* mask, void* out, int dtype,
+                       int64_t B, int64_t H, int64_t L, int64_t D, float scale, void* stream) {
+  if (B < 0 || H < 0 || L < 0 || D <= 0) return fail(MTP_ERR_SHAPE, "bad attention sizes");
+  if (!valid_dtype(dtype) || dtype == MTP_DTYPE_E4M3) return fail(MTP_ERR_DTYPE, "unsupported dtype %d", dtype);
+  if (B * H == 0) return MTP_OK;
+  if (!q || !out || (L > 0 && (!k || !v))) return fail(MTP_ERR_ARG, "null tensor pointer");
+  AttnArgs a{};
+  a.kind = ATTN_CONTIG;
+  a.dtype = dtype;
+  a.q = q;
+  a.out = out;
+  a.B = B;
+  a.T = 1;
+  a.Hq = H;
+  a.Hkv = H;
+  a.D = D;
+  a.scale = scale;
+  a.k = k;
+  a.v = v;
+  a.mask = mask;
+  a.L = L;
+  return launch_decode_attention(a, as_stream(stream));
+}
+
+int mtp_paged_attention(const void* q, const void* k_pages, const void* v_pages, const int32_t* page_table,
+                        void* out, int dtype, int64_t B, int64_t H, int64_t L, int64_t D, int64_t num_pages,
+                        int64_t page_size, float scale, void* stream) {
+  if (B < 0 || H < 0 || L < 0 || D <= 0 || page_size <= 0 || num_pages < 0)
+    return fail(MTP_ERR_SHAPE, "bad paged attention sizes");
+  if (!valid_dtype(dtype) || dtype == MTP_DTYPE_E4M3) return fail(MTP_ERR_DTYPE, "unsupported dtype %d", dtype);
+  if (B * H == 0) return MTP_OK;
+  if (!q || !out || (L > 0 && (!k_pages || !v_pages || !page_table))) return fail(MTP_ERR_ARG, "null tensor pointer");
+  AttnArgs a{};
+  a.kind = ATTN_PAGED;
+  a.dtype = dtype;
+  a.q = q;
+  a.out = out;
+  a.B = B;
+  a.T = 1;
+  a.Hq = H;
+  a.Hkv = H;
+  a.D = D;
+  a.scale = scale;
+  a.L = L;
+  a.k_pages = k_pages;
+  a.v_pages = v_pages;
+  a.page_table = page_table;
+  a.table_stride = L;
+  a.num_pages = num_pages;
+  a.page_size = page_size;
+  a.ctx_len = L;
+  return launch_decode_attention(a, as_stream(stream));
+}
+
+size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
+                                          int64_t ctx_len) {
+  (void)B, (void)T, (void)Hq, (void)Hkv, (void)D, (void)ctx_len;
+  return 256;
+}
+
+int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_pages, const int32_t* page_table,
+                             int64_t table_stride, int64_t ctx_len, const void* tree_k, const void* tree_v,
+                             const float* tree_mask, void* out, int dtype, int64_t B, int64_t T, int64_t Hq,
+                             int64_t Hkv, int64_t D, int64_t num_pages, int64_t page_size, float scale,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace, (void)workspace_bytes;
+  if (B < 0 || T < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || ctx_len < 0 || page_size <= 0 || num_pages < 0)
+    return fail(MTP_ERR_SHAPE, "bad tree attention sizes");
+  if (Hq % Hkv != 0) return fail(MTP_ERR_SHAPE, "Hq=%lld not a multiple of Hkv=%lld", (long long)Hq, (long long)Hkv);
+  if (table_stride < ctx_len) return fail(MTP_ERR_SHAPE, "page table narrower than ctx_len");
+  if (!valid_dtype(dtype) || dtype == MTP_DTYPE_E4M3) return fail(MTP_ERR_DTYPE, "unsupported dtype %d", dtype);
+  if (B * T == 0) return MTP_OK;
+  if (!q || !out || !tree_k || !tree_v || !tree_mask || (ctx_len > 0 && (!k_pages || !v_pages || !page_table)))
+    return fail(MTP_ERR_ARG, "null tensor pointer");
+  AttnArgs a{};
+  a.kind = ATTN_TREE_PAGED;
+  a.dtype = dtype;
+  a.q = q;
+  a.out = out;
+  a.B = B;
+  a.T = T;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = D;
+  a.scale = scale;
+  a.k_pages = k_pages;
+  a.v_pages = v_pages;
+  a.page_table = page_table;
+  a.table_stride = table_stride;
+  a.num_pages = num_pages;
+  a.page_size = page_size;
+  a.ctx_len = ctx_len;
+  a.tree_k = tree_k;
+  a.tree_v = tree_v;
+  a.tree_mask = tree_mask;
+  return launch_decode_attention(a, as_stream(stream));
+}
+
+// ---------------------------------------------------------------- verify
+size_t mtp_verify_workspace(int64_t rows) { return verify_ws_bytes(rows < 0 ? 0 : rows); }
+
+int mtp_keys_fill(int64_t* keys, int64_t n, void* stream) {
+  if (n <= 0) return MTP_OK;
+  if (!keys) return fail(MTP_ERR_ARG, "null keys");
+  keys_fill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, as_stream(stream)>>>(reinterpret_cast<long long*>(keys),
+                                                                               n, nullptr);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+int mtp_verify_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < 256) return fail(MTP_ERR_WORKSPACE, "workspace too small");
+  const int64_t rows = (int64_t)((workspace_bytes - 256) / 8);
+  long long* keys = static_cast<long long*>(workspace);
+  unsigned int* counter = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + workspace_bytes - 256);
+  const int64_t n = rows > 0 ? rows : 1;
+  keys_fill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, as_stream(stream)>>>(keys, rows, counter);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+static int verify_common(const void* hidden, int h_dtype, const void* weight, int w_dtype, const void* bias,
+                         int bias_dtype, int64_t rows, int64_t K, int64_t V, void* workspace,
+                         size_t workspace_bytes, GemmEpilogue& ep, cudaStream_t s) {
+  if (int st = check_dims(rows, V, K)) return st;
+  if (V == 0) return fail(MTP_ERR_SHAPE, "empty vocabulary");
+  if (!valid_dtype(h_dtype) || !valid_dtype(w_dtype) || h_dtype == MTP_DTYPE_E4M3 || w_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtype combination hidden=%d weight=%d", h_dtype, w_dtype);
+  if (!hidden || !weight) return fail(MTP_ERR_ARG, "null tensor pointer");
+  const size_t need = verify_ws_bytes(rows);
+  if (!workspace || workspace_bytes < need) return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  ep.mode = EPI_ARGMAX;
+  ep.bias = bias;
+  ep.bias_dtype = bias_dtype;
+  ep.keys = static_cast<long long*>(workspace);
+  ep.col_offset = 0;
+  // the counter sits in the last 256 bytes of the workspace the caller sized
+  ep.counter = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + workspace_bytes - 256);
+  return launch_gemm(hidden, h_dtype, weight, w_dtype, rows, V, K, ep, s);
+}
+
+int mtp_fused_verify(const void* hidden, int h_dtype, const void* weight, int w_dtype, const void* bias,
+                     int bias_dtype, const int32_t* draft, int8_t* accept, int32_t* top, int64_t M, int64_t K,
+                     int64_t V, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M == 0) return MTP_OK;
+  if (!draft || !accept || !top) return fail(MTP_ERR_ARG, "null output pointer");
+  GemmEpilogue ep{};
+  ep.finalize = FIN_SINGLE;
+  ep.draft = draft;
+  ep.accept = accept;
+  ep.tokens = top;
+  ep.B = M;
+  ep.S = 1;
+  return verify_common(hidden, h_dtype, weight, w_dtype, bias, bias_dtype, M, K, V, workspace, workspace_bytes, ep,
+                       as_stream(stream));
+}
+
+int mtp_fused_multi_verify(const void* hidden, int h_dtype, const void* weight, int w_dtype, const void* bias,
+                           int bias_dtype, const int32_t* draft, int8_t* accept, int32_t* accepted_n,
+                           int32_t* corrected, int64_t B, int64_t S, int64_t K, int64_t V, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1 (S == D + 1), got S=%lld", (long long)S);
+  if (B == 0) return MTP_OK;
+  if ((S > 1 && (!draft || !accept)) || !accepted_n || !corrected) return fail(MTP_ERR_ARG, "null output pointer");
+  GemmEpilogue ep{};
+  ep.finalize = FIN_CHAIN;
+  ep.draft = draft;
+  ep.accept = accept;
+  ep.accepted_n = accepted_n;
+  ep.tokens = corrected;
+  ep.B = B;
+  ep.S = S;
+  return verify_common(hidden, h_dtype, weight, w_dtype, bias, bias_dtype, B * S, K, V, workspace,
+                       workspace_bytes, ep, as_stream(stream));
+}
+
+int mtp_verify_shard_keys(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                          const void* bias_shard, int bias_dtype, int64_t* keys, int64_t M, int64_t K,
+                          int64_t V_shard, int64_t vocab_offset, void* stream) {
+  if (int st = check_dims(M, V_shard, K)) return st;
+  if (M == 0 || V_shard == 0) return MTP_OK;
+  if (vocab_offset < 0 || vocab_offset + V_shard > 0xFFFFFFFFLL) return fail(MTP_ERR_SHAPE, "vocab offset out of range");
+  if (!valid_dtype(h_dtype) || !valid_dtype(w_dtype) || h_dtype == MTP_DTYPE_E4M3 || w_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtype combination hidden=%d weight=%d", h_dtype, w_dtype);
+  if (!hidden || !weight_shard || !keys) return fail(MTP_ERR_ARG, "null tensor pointer");
+  GemmEpilogue ep{};
+  ep.mode = EPI_ARGMAX;
+  ep.bias = bias_shard;
+  ep.bias_dtype = bias_dtype;
+  ep.keys = reinterpret_cast<long long*>(keys);
+  ep.col_offset = vocab_offset;
+  ep.finalize = FIN_NONE;
+  return launch_gemm(hidden, h_dtype, weight_shard, w_dtype, M, V_shard, K, ep, as_stream(stream));
+}
+
+int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* accept, int32_t* accepted_n,
+                               int32_t* corrected, int64_t B, int64_t S, void* stream) {
+  if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1");
+  if (B == 0) return MTP_OK;
+  if (!keys || (S > 1 && (!draft || !accept)) || !accepted_n || !corrected) return fail(MTP_ERR_ARG, "null pointer");
+  GemmEpilogue ep{};
+  ep.mode = EPI_ARGMAX;
+  ep.keys = reinterpret_cast<long long*>(keys);
+  ep.finalize = FIN_CHAIN;
+  ep.draft = draft;
+  ep.accept = accept;
+  ep.accepted_n = accepted_n;
+  ep.tokens = corrected;
+  ep.B = B;
+  ep.S = S;
+  const unsigned blocks = (unsigned)((B + 127) / 128);
+  verify_finalize_kernel<<<blocks, 128, 0, as_stream(stream)>>>(ep);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+}  // extern "C"

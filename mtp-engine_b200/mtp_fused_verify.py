@@ -1,0 +1,92 @@
+"""B200-native drop-in for the reference's ``mtp_fused_verify`` module.
+
+``fused_verify`` (mtp_fused_verify.py:199-234) and ``fused_multi_verify``
+(mtp_fused_verify.py:237-290) keep their signatures and return tuples.
+One kernel launch per call: a tcgen05 lm_head GEMM whose epilogue reduces
+every logit row to a packed (value, index) argmax key -- no logits tensor
+is ever written -- and whose last CTA decodes the keys into the acceptance
+outputs.  bf16/f16 hidden + weight run on the tensor cores with fp32
+accumulation; fp32 inputs run an IEEE fp32 CUDA-core GEMM, matching the
+reference's fp32 logits (mtp_fused_verify.py:179-181).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+import _mtp_native as _N
+
+
+def _prep(hidden, weight, draft, bias):
+    hidden = hidden.contiguous()
+    weight = weight.contiguous()
+    draft = draft.contiguous().to(torch.int32)
+    dev = _N.require_cuda(hidden, weight, draft, bias)
+    if bias is not None:
+        bias = bias.contiguous()
+        assert bias.numel() == weight.shape[0]
+    return hidden, weight, draft, bias, dev
+
+
+def fused_verify(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    draft: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """top[m] = argmax(hidden[m] @ weight.T + bias); accept[m] = top[m] == draft[m].
+    hidden [M,K], weight [V,K], draft [M] -> (accept int8 [M], top int32 [M])."""
+    hidden, weight, draft, bias, dev = _prep(hidden, weight, draft, bias)
+    M, K = hidden.shape
+    V = weight.shape[0]
+    assert weight.shape[1] == K and draft.numel() == M
+    accept = torch.empty(M, dtype=torch.int8, device=hidden.device)
+    top = torch.empty(M, dtype=torch.int32, device=hidden.device)
+    if M == 0:
+        return accept, top
+    ws = _N.verify_workspace(dev, M)
+    _N.check(_N.lib().mtp_fused_verify(
+        _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight), _N.dtype_code(weight),
+        _N.ptr(bias), _N.dtype_code(bias) if bias is not None else 0,
+        _N.ptr(draft), _N.ptr(accept), _N.ptr(top), M, K, V, _N.ptr(ws), ws.numel(),
+        _N.stream_handle(dev)), "fused_verify")
+    return accept, top
+
+
+def fused_multi_verify(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    draft: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Linear -> argmax -> prefix-gated chain acceptance for a draft chain.
+
+    hidden [B,S,K] (anchor + D drafts, S == D + 1); weight [V,K];
+    draft [B,D]; bias [V] or None.  Returns
+      accept     [B,D] int8  (1 while every earlier draft was accepted too)
+      accepted_n [B]   int32 (accepted prefix length = rollback index)
+      corrected  [B]   int32 (argmax at the anchor position 0)
+    """
+    hidden, weight, draft, bias, dev = _prep(hidden, weight, draft, bias)
+    B, S, K = hidden.shape
+    V = weight.shape[0]
+    D = draft.shape[1]
+    assert S == D + 1, f"expected S == D + 1, got S={S} D={D}"
+    assert weight.shape[1] == K and draft.shape[0] == B
+    accept = torch.empty((B, D), dtype=torch.int8, device=hidden.device)  # fully written
+    accepted_n = torch.empty((B,), dtype=torch.int32, device=hidden.device)
+    corrected = torch.empty((B,), dtype=torch.int32, device=hidden.device)
+    if B == 0:
+        return accept, accepted_n, corrected
+    ws = _N.verify_workspace(dev, B * S)
+    _N.check(_N.lib().mtp_fused_multi_verify(
+        _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight), _N.dtype_code(weight),
+        _N.ptr(bias), _N.dtype_code(bias) if bias is not None else 0,
+        _N.ptr(draft), _N.ptr(accept), _N.ptr(accepted_n), _N.ptr(corrected),
+        B, S, K, V, _N.ptr(ws), ws.numel(), _N.stream_handle(dev)), "fused_multi_verify")
+    return accept, accepted_n, corrected
+
+
+__all__ = ["fused_verify", "fused_multi_verify"]

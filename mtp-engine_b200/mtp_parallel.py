@@ -1,0 +1,248 @@
+"""Vocab-parallel verification for the reference's ``mtp_parallel`` module.
+
+The lm_head W [V, K] is split into contiguous row blocks, one per rank,
+exactly as ``torch.chunk(W, tp, dim=0)`` splits it (the scatter of
+ParallelPrimitives, mtp_parallel.py:62-66; RowParallelLinear holds
+out_features // tp rows per rank, mtp_parallel.py:96-101).  Instead of
+gathering [B, S, V/tp] fp32 logits from every rank (RowParallelLinear with
+gather_output, mtp_parallel.py:114-118), each rank reduces its block to one
+packed int64 key per logit row,
+
+    key = (signed-ordered fp32 max logit << 32) | (0xFFFFFFFF - global index),
+
+so a single all-reduce(MAX) of B*S int64 keys (3 KB at B=64, S=6) yields
+the global argmax with torch.argmax's lowest-index tie rule, after which
+every rank decodes identical (accept, accepted_n, corrected).  The
+collective is torch.distributed (NCCL over NVLink on a B200 node, gloo on
+CPU test ranks).
+
+Also provided for drop-in compatibility: ParallelPrimitives /
+get_parallel_primitives (same properties and collectives as
+mtp_parallel.py:12-81) and RowParallelLinear (vocab-sharded linear,
+mtp_parallel.py:84-118) with an added ``verify`` method.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import _mtp_native as _N
+
+
+class ParallelPrimitives:
+    """World/rank lookup and the three collectives of the reference
+    (sum all-reduce, all-gather + concat, local chunk), mtp_parallel.py:12-66."""
+
+    def __init__(self, group: Optional[object] = None):
+        self._group = group
+
+    @property
+    def dist(self):
+        d = torch.distributed
+        return d if d.is_available() and d.is_initialized() else None
+
+    @property
+    def initialized(self) -> bool:
+        return self.dist is not None
+
+    @property
+    def world_size(self) -> int:
+        return int(self.dist.get_world_size(self._group)) if self.initialized else 1
+
+    @property
+    def rank(self) -> int:
+        return int(self.dist.get_rank(self._group)) if self.initialized else 0
+
+    @property
+    def tp_size(self) -> int:
+        return self.world_size
+
+    @property
+    def group(self):
+        return self._group
+
+    def all_reduce(self, x: torch.Tensor, op=None) -> torch.Tensor:
+        if self.tp_size > 1:
+            if op is None:
+                self.dist.all_reduce(x, group=self._group)
+            else:
+                self.dist.all_reduce(x, op=op, group=self._group)
+        return x
+
+    def all_gather(self, x: torch.Tensor, dim: int) -> torch.Tensor:
+        if self.tp_size <= 1:
+            return x
+        parts = [torch.empty_like(x) for _ in range(self.tp_size)]
+        self.dist.all_gather(parts, x, group=self._group)
+        return torch.cat(parts, dim=dim)
+
+    def scatter(self, x: torch.Tensor, dim: int, shard_size: Optional[int] = None) -> torch.Tensor:
+        if self.tp_size <= 1:
+            return x
+        return torch.chunk(x, self.tp_size, dim=dim)[self.rank].contiguous()
+
+
+_PRIMITIVES: Optional[ParallelPrimitives] = None
+
+
+def get_parallel_primitives(group: Optional[object] = None) -> ParallelPrimitives:
+    global _PRIMITIVES
+    if _PRIMITIVES is None:
+        _PRIMITIVES = ParallelPrimitives(group)
+    return _PRIMITIVES
+
+
+def _reset_parallel_primitives() -> None:
+    global _PRIMITIVES
+    _PRIMITIVES = None
+
+
+def vocab_shard_range(vocab_size: int, world: int, rank: int) -> Tuple[int, int]:
+    """[lo, hi) rows of rank `rank` under torch.chunk(W, world, dim=0)."""
+    step = -(-vocab_size // world)
+    lo = min(rank * step, vocab_size)
+    return lo, min(lo + step, vocab_size)
+
+
+def shard_lm_head(weight: torch.Tensor, world: int, rank: int) -> Tuple[torch.Tensor, int]:
+    """This rank's contiguous vocabulary block of a full lm_head and its offset."""
+    lo, hi = vocab_shard_range(weight.shape[0], world, rank)
+    return weight[lo:hi].contiguous(), lo
+
+
+_KEYS_WS = "vocab_parallel_keys"
+
+
+def _keys_buffer(dev: torch.device, rows: int) -> torch.Tensor:
+    L = _N.lib()
+
+    def _init(buf):
+        _N.check(L.mtp_keys_fill(_N.ptr(buf), buf.numel() // 8, _N.stream_handle(dev)), "mtp_keys_fill")
+
+    buf = _N.workspace(dev, _KEYS_WS, rows * 8, _init)
+    return buf[: rows * 8].view(torch.int64)
+
+
+def vocab_parallel_multi_verify(
+    hidden: torch.Tensor,
+    weight_shard: torch.Tensor,
+    draft: torch.Tensor,
+    bias_shard: Optional[torch.Tensor] = None,
+    vocab_offset: Optional[int] = None,
+    prim: Optional[ParallelPrimitives] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``fused_multi_verify`` with the lm_head split over the ranks of `prim`.
+
+    hidden [B,S,K] and draft [B,S-1] are replicated; weight_shard
+    [V_r, K] / bias_shard [V_r] are this rank's rows, starting at global row
+    `vocab_offset` (default: the torch.chunk offset of this rank, assuming
+    equal shards).  Every rank returns the same (accept, accepted_n,
+    corrected) as single-device ``fused_multi_verify`` on the full weight.
+    """
+    prim = prim or get_parallel_primitives()
+    hidden = hidden.contiguous()
+    weight_shard = weight_shard.contiguous()
+    draft = draft.contiguous().to(torch.int32)
+    dev = _N.require_cuda(hidden, weight_shard, draft, bias_shard)
+    if bias_shard is not None:
+        bias_shard = bias_shard.contiguous()
+    B, S, K = hidden.shape
+    D = draft.shape[1]
+    assert S == D + 1, f"expected S == D + 1, got S={S} D={D}"
+    Vr = weight_shard.shape[0]
+    if vocab_offset is None:
+        vocab_offset = prim.rank * Vr
+    rows = B * S
+    accept = torch.empty((B, D), dtype=torch.int8, device=hidden.device)
+    accepted_n = torch.empty((B,), dtype=torch.int32, device=hidden.device)
+    corrected = torch.empty((B,), dtype=torch.int32, device=hidden.device)
+    L = _N.lib()
+    keys = _keys_buffer(dev, rows)  # at rest: every key is INT64_MIN
+    stream = _N.stream_handle(dev)
+    try:
+        _N.check(L.mtp_verify_shard_keys(
+            _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight_shard), _N.dtype_code(weight_shard),
+            _N.ptr(bias_shard), _N.dtype_code(bias_shard) if bias_shard is not None else 0,
+            _N.ptr(keys), rows, K, Vr, int(vocab_offset), stream), "mtp_verify_shard_keys")
+        if prim.tp_size > 1:
+            prim.all_reduce(keys, op=torch.distributed.ReduceOp.MAX)
+        _N.check(L.mtp_verify_chain_from_keys(
+            _N.ptr(keys), _N.ptr(draft), _N.ptr(accept), _N.ptr(accepted_n), _N.ptr(corrected), B, S, stream),
+            "mtp_verify_chain_from_keys")  # also puts the keys back to rest
+    except Exception:
+        _N.drop_workspace(dev, _KEYS_WS)  # never reuse keys left mid-reduction
+        raise
+    return accept, accepted_n, corrected
+
+
+class VocabParallelVerify:
+    """Callable holding one rank's lm_head shard: ``__call__(hidden, draft)``
+    returns the replicated (accept, accepted_n, corrected)."""
+
+    def __init__(self, weight_shard: torch.Tensor, vocab_offset: Optional[int] = None,
+                 bias_shard: Optional[torch.Tensor] = None, prim: Optional[ParallelPrimitives] = None):
+        self.prim = prim or get_parallel_primitives()
+        self.weight_shard = weight_shard.contiguous()
+        self.bias_shard = None if bias_shard is None else bias_shard.contiguous()
+        self.vocab_offset = self.prim.rank * self.weight_shard.shape[0] if vocab_offset is None else vocab_offset
+
+    @classmethod
+    def from_full(cls, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                  prim: Optional[ParallelPrimitives] = None) -> "VocabParallelVerify":
+        prim = prim or get_parallel_primitives()
+        w, off = shard_lm_head(weight, prim.tp_size, prim.rank)
+        b = None if bias is None else bias[off:off + w.shape[0]]
+        return cls(w, off, b, prim)
+
+    def __call__(self, hidden: torch.Tensor, draft: torch.Tensor,
+                 bias_shard: Optional[torch.Tensor] = None):
+        b = self.bias_shard if bias_shard is None else bias_shard
+        return vocab_parallel_multi_verify(hidden, self.weight_shard, draft, b, self.vocab_offset, self.prim)
+
+
+class RowParallelLinear(nn.Module):
+    """Linear layer whose out_features (the vocabulary) are split over the
+    ranks, as in mtp_parallel.py:84-118: forward() returns this rank's
+    logits, all-gathered when gather_output else sum-all-reduced (the
+    reference's default).  ``verify`` runs the fused vocab-parallel
+    verification on the shard without materialising logits."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, gather_output: bool = False,
+                 prim: Optional[ParallelPrimitives] = None):
+        super().__init__()
+        self.prim = prim if prim is not None else get_parallel_primitives()
+        tp = self.prim.tp_size
+        assert out_features % tp == 0
+        self.in_features = in_features
+        self.out_features = out_features
+        self.out_features_per_rank = out_features // tp
+        self.gather_output = gather_output
+        self.weight = nn.Parameter(torch.empty(self.out_features_per_rank, in_features))
+        self.bias = nn.Parameter(torch.empty(self.out_features_per_rank)) if bias else None
+        self.reset_parameters()
+
+    def reset_parameters(self) -> None:
+        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
+        if self.bias is not None:
+            bound = 1.0 / math.sqrt(self.in_features)
+            nn.init.uniform_(self.bias, -bound, bound)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        y = F.linear(x, self.weight, self.bias)
+        return self.prim.all_gather(y, dim=-1) if self.gather_output else self.prim.all_reduce(y)
+
+    @torch.no_grad()
+    def verify(self, hidden: torch.Tensor, draft: torch.Tensor):
+        off = self.prim.rank * self.out_features_per_rank
+        return vocab_parallel_multi_verify(hidden, self.weight, draft, self.bias, off, self.prim)
+
+
+__all__ = [
+    "ParallelPrimitives", "get_parallel_primitives", "vocab_shard_range", "shard_lm_head",
+    "vocab_parallel_multi_verify", "VocabParallelVerify", "RowParallelLinear",
+]

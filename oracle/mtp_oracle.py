@@ -286,6 +286,35 @@ def tree_attention_paged(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray
     return out
 
 
+def tree_attention_paged_fast(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray,
+                              page_table: np.ndarray, ctx_len: int, page_size: int,
+                              tree_k: np.ndarray, tree_v: np.ndarray, tree_mask: np.ndarray,
+                              scale: float) -> np.ndarray:
+    """Same result as ``tree_attention_paged`` (checked by the CPU tests),
+    computed per (b, kv head) with one BLAS matmul over all T*G query rows --
+    the form the CPU baseline of bench.py times."""
+    qf = np.asarray(q, dtype=np.float32)
+    B, T, Hq, D = qf.shape
+    Hkv = tree_k.shape[1]
+    G = Hq // Hkv
+    Tk = tree_k.shape[2]
+    kc = gather_paged_kv(k_pages, page_table, page_size, ctx_len).astype(np.float32)
+    vc = gather_paged_kv(v_pages, page_table, page_size, ctx_len).astype(np.float32)
+    keep = np.concatenate([np.ones((T, ctx_len), bool), np.asarray(tree_mask)[:, :Tk] > 0.5], axis=1)
+    out = np.empty((B, T, Hq, D), dtype=np.float32)
+    for b in range(B):
+        for h in range(Hkv):
+            K = np.concatenate([kc[b, h], np.asarray(tree_k[b, h], np.float32)], axis=0)  # [L+T, D]
+            V = np.concatenate([vc[b, h], np.asarray(tree_v[b, h], np.float32)], axis=0)
+            Q = qf[b, :, h * G:(h + 1) * G, :].reshape(T * G, D)  # rows (t, g)
+            s = (Q @ K.T) * np.float32(scale)
+            s = np.where(np.repeat(keep, G, axis=0), s, np.float32(-np.inf))
+            with np.errstate(invalid="ignore"):
+                p = _softmax_rows(s)
+            out[b, :, h * G:(h + 1) * G, :] = (p @ V).reshape(T, G, D)
+    return out
+
+
 # --------------------------------------------------------------------------- #
 # speculative draft tree (mask contract)
 # --------------------------------------------------------------------------- #

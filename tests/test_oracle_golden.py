@@ -156,6 +156,10 @@ def test_tree_paged_attention(golden):
                                g["tree_k"], g["tree_v"], g["tree_mask"],
                                1.0 / math.sqrt(g["q"].shape[-1]))
     np.testing.assert_allclose(o, g["out"], rtol=1e-5, atol=1e-5)
+    of = O.tree_attention_paged_fast(g["q"], g["k_pages"], g["v_pages"], g["page_table"], ctx, ps,
+                                     g["tree_k"], g["tree_v"], g["tree_mask"],
+                                     1.0 / math.sqrt(g["q"].shape[-1]))
+    np.testing.assert_allclose(of, g["out"], rtol=1e-5, atol=1e-5)
 
 
 @pytest.mark.parametrize("key,args", [("tree_16_4", (16, 4, "tree")), ("tree_4_8", (4, 8, "tree")),
