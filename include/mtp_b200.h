@@ -196,6 +196,13 @@ int mtp_keys_fill(int64_t* keys, int64_t n, void* stream);
  * devices).  Benchmarks read it around a timed region. */
 uint64_t mtp_launch_count(void);
 
+/* Test support (no counterpart in the reference): C[M,N] (fp32) = A[M,K] @ B[N,K]^T
+ * through the GEMM mainloop the operators use -- the tcgen05 kernel when
+ * force_simt == 0 and the operands qualify (bf16/f16/E4M3, 16-byte rows),
+ * else the fp32 CUDA-core kernel. */
+int mtp_gemm_test(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,
+                  int force_simt, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,7 @@ SIGNATURES = {
     "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
     "mtp_launch_count": (ctypes.c_uint64, []),
+    "mtp_gemm_test": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _i, _vp]),
 }
 
 _lib = None

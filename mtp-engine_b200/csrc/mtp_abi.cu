@@ -223,6 +223,18 @@ const char* mtp_last_error(void) { return g_err; }
 
 uint64_t mtp_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int mtp_gemm_test(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,
+                  int force_simt, void* stream) {
+  if (int st = check_dims(M, N, K)) return st;
+  if (!valid_dtype(ab_dtype)) return fail(MTP_ERR_DTYPE, "bad dtype");
+  if (M == 0 || N == 0) return MTP_OK;
+  if (!A || !B || !C) return fail(MTP_ERR_ARG, "null pointer");
+  GemmEpilogue ep = store_epilogue(nullptr, nullptr, nullptr, 0, 1.0f, C, MTP_DTYPE_F32, N);
+  if (!force_simt && tc_eligible(A, B, ab_dtype, ab_dtype, M, N, K))
+    return launch_gemm_tc(A, B, ab_dtype, ab_dtype == MTP_DTYPE_E4M3, M, N, K, ep, as_stream(stream));
+  return launch_gemm_simt(A, ab_dtype, B, ab_dtype, M, N, K, ep, as_stream(stream));
+}
+
 int mtp_device_status(void* stream, int* code_out, int clear) {
   MTP_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
   int code = 0;

@@ -20,8 +20,9 @@ namespace mtp {
 
 enum RowMode : int { ROW_RSTD = 0, ROW_GAMMA = 1, ROW_QUANT = 2, ROW_PREQUANT = 3 };
 
+// Block-wide reduction; `identity` fills the lanes beyond the warp count.
 template <typename Op>
-__device__ __forceinline__ float block_reduce(float v, Op op, float* red) {
+__device__ __forceinline__ float block_reduce(float v, Op op, float identity, float* red) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, off));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -29,7 +30,7 @@ __device__ __forceinline__ float block_reduce(float v, Op op, float* red) {
   if (lane == 0) red[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    v = lane < (int)(blockDim.x >> 5) ? red[lane] : red[0];
+    v = lane < (int)(blockDim.x >> 5) ? red[lane] : identity;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, off));
     if (lane == 0) red[0] = v;
@@ -58,7 +59,7 @@ __global__ void __launch_bounds__(256)
       ss = fmaf(v, v, ss);
       if (mode == ROW_GAMMA) store_f32(xo, xo_dt, base + k, v * load_f32(gamma, g_dt, k));
     }
-    ss = block_reduce(ss, AddOp(), red);
+    ss = block_reduce(ss, AddOp(), 0.0f, red);
     if (threadIdx.x == 0) row_out[row] = 1.0f / sqrtf(ss / (float)K + eps);
     return;
   }
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(256)
   if (mode == ROW_QUANT) {
     float amax = 0.f;
     for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(load_f32(x, x_dt, base + k)));
-    amax = block_reduce(amax, MaxOp(), red);
+    amax = block_reduce(amax, MaxOp(), 0.0f, red);
     sx = amax > 0.f ? amax / 448.0f : 1.0f;
     for (int k = threadIdx.x; k < K; k += blockDim.x) {
       const float v = fminf(fmaxf(load_f32(x, x_dt, base + k) / sx, -448.0f), 448.0f);
@@ -84,7 +85,7 @@ __global__ void __launch_bounds__(256)
       ss = fmaf(d, d, ss);
     }
   }
-  ss = block_reduce(ss, AddOp(), red);
+  ss = block_reduce(ss, AddOp(), 0.0f, red);
   if (threadIdx.x == 0) row_out[row] = sx * (1.0f / sqrtf(ss / (float)K + eps));
 }
 
