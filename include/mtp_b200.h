@@ -189,6 +189,29 @@ int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* acce
                                int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S,
                                void* stream);
 
+/* Largest B*S that mtp_fused_multi_verify_noalloc accepts. */
+#define MTP_NOALLOC_MAX_ROWS 8192
+
+/* Chain verification that allocates nothing and takes no workspace.
+ * It has no counterpart in the reference.  It exists for callers that
+ * cannot hand the library scratch memory: a host whose device memory is
+ * already claimed up front by another allocator (for example a serving
+ * process that reserved the free HBM for its KV cache), or a plain C/FFI
+ * host that owns only its input and output buffers and must not call
+ * cudaMalloc (which can synchronise the device) in the middle of a step.
+ * Same inputs, outputs and results as mtp_fused_multi_verify.  Its keys and
+ * ticket live in one fixed array of MTP_NOALLOC_MAX_ROWS * 8 + 256 bytes
+ * inside the library, which every GPU that loads the library keeps until
+ * the process exits; B*S above MTP_NOALLOC_MAX_ROWS is rejected with
+ * MTP_ERR_SHAPE.  The first call on a device looks up that array's device
+ * address (make that first call before any stream capture).  Each call
+ * clears the array first; all calls on a device share it, so calls whose
+ * kernels overlap on the GPU (different streams, no ordering) race. */
+int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* weight, int w_dtype,
+                                   const void* bias, int bias_dtype, const int32_t* draft, int8_t* accept,
+                                   int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S, int64_t K,
+                                   int64_t V, void* stream);
+
 /* Fills keys[n] with INT64_MIN. */
 int mtp_keys_fill(int64_t* keys, int64_t n, void* stream);
 

@@ -19,6 +19,12 @@
 
 using namespace mtp;
 
+// Scratch of mtp_fused_multi_verify_noalloc: MTP_NOALLOC_MAX_ROWS int64 keys,
+// then the last-CTA ticket counter in the final 256 bytes.  A module-scope
+// device array, so the library never allocates it; in host code its name is
+// only a stand-in -- its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MTP_NOALLOC_MAX_ROWS * 8 + 256];
+
 namespace {
 
 constexpr int kAbiVersion = 1;
@@ -211,6 +217,25 @@ int check_dims(int64_t M, int64_t N, int64_t K) {
 }
 
 size_t verify_ws_bytes(int64_t rows) { return align256((size_t)rows * 8) + 256; }
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(unsigned char** out) {
+  static std::mutex mu;
+  static unsigned char* cache[kMaxDevices] = {nullptr};
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(MTP_ERR_CUDA, "cudaGetSymbolAddress(no-allocation scratch) failed: %s", cudaGetErrorString(e));
+    cache[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = cache[dev];
+  return MTP_OK;
+}
 
 }  // namespace
 
@@ -513,6 +538,49 @@ int mtp_fused_multi_verify(const void* hidden, int h_dtype, const void* weight, 
   ep.S = S;
   return verify_common(hidden, h_dtype, weight, w_dtype, bias, bias_dtype, B * S, K, V, workspace,
                        workspace_bytes, ep, as_stream(stream));
+}
+
+// Same computation as mtp_fused_multi_verify with the library's fixed scratch
+// array in place of a caller workspace; allocates nothing.
+int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* weight, int w_dtype,
+                                   const void* bias, int bias_dtype, const int32_t* draft, int8_t* accept,
+                                   int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S, int64_t K,
+                                   int64_t V, void* stream) {
+  if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1 (S == D + 1), got S=%lld", (long long)S);
+  if (B == 0) return MTP_OK;
+  const int64_t rows = B * S;
+  if (rows > MTP_NOALLOC_MAX_ROWS)
+    return fail(MTP_ERR_SHAPE, "B*S=%lld exceeds the %d rows of the no-allocation scratch; use mtp_fused_multi_verify",
+                (long long)rows, MTP_NOALLOC_MAX_ROWS);
+  if (int st = check_dims(rows, V, K)) return st;
+  if (V == 0) return fail(MTP_ERR_SHAPE, "empty vocabulary");
+  if (!valid_dtype(h_dtype) || !valid_dtype(w_dtype) || h_dtype == MTP_DTYPE_E4M3 || w_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtype combination hidden=%d weight=%d", h_dtype, w_dtype);
+  if (!hidden || !weight) return fail(MTP_ERR_ARG, "null tensor pointer");
+  if ((S > 1 && (!draft || !accept)) || !accepted_n || !corrected) return fail(MTP_ERR_ARG, "null output pointer");
+  unsigned char* scratch = nullptr;
+  if (int st = noalloc_scratch(&scratch)) return st;
+  long long* keys = reinterpret_cast<long long*>(scratch);
+  unsigned int* counter = reinterpret_cast<unsigned int*>(scratch + (size_t)MTP_NOALLOC_MAX_ROWS * 8);
+  cudaStream_t s = as_stream(stream);
+  // the array still holds whatever the previous call left: clear keys and ticket
+  keys_fill_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(keys, rows, counter);
+  MTP_LAUNCH_CHECK();
+  GemmEpilogue ep{};
+  ep.mode = EPI_ARGMAX;
+  ep.bias = bias;
+  ep.bias_dtype = bias_dtype;
+  ep.keys = keys;
+  ep.col_offset = 0;
+  ep.counter = counter;
+  ep.finalize = FIN_CHAIN;
+  ep.draft = draft;
+  ep.accept = accept;
+  ep.accepted_n = accepted_n;
+  ep.tokens = corrected;
+  ep.B = B;
+  ep.S = S;
+  return launch_gemm(hidden, h_dtype, weight, w_dtype, rows, V, K, ep, s);
 }
 
 int mtp_verify_shard_keys(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
