@@ -12,6 +12,7 @@
 #include <stdio.h>
 
 #include "mtp_attention.cuh"
+#include "mtp_attention_tc.cuh"
 #include "mtp_gemm_simt.cuh"
 #include "mtp_gemm_tc.cuh"
 #include "mtp_rownorm.cuh"
@@ -418,10 +419,167 @@ int mtp_paged_attention(const void* q, const void* k_pages, const void* v_pages,
   return launch_decode_attention(a, as_stream(stream));
 }
 
+}  // extern "C"
+
+namespace {
+
+// Shape plan of the tensor-core tree attention; eligible == false -> CUDA-core kernel.
+struct TreePlan {
+  bool eligible = false;
+  int G = 0, n_tiles = 0, t_per_tile = 0, n_ctx_chunks = 0, n_chunks = 0, splits = 1, chunks_per_split = 0;
+  size_t ws_bytes = 256;
+};
+
+TreePlan tree_plan(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t ctx_len, int64_t page_size,
+                   int64_t num_pages, int dtype) {
+  TreePlan pl;
+  if (!(dtype == MTP_DTYPE_BF16 || dtype == MTP_DTYPE_F16) || D != attn::kD || Hkv <= 0 || Hq % Hkv) return pl;
+  const int64_t G = Hq / Hkv;
+  if (G <= 0 || attn::kChunk % G != 0 || T < 1 || T * G > 256) return pl;
+  if (!(page_size == 8 || page_size == 16 || page_size == 32 || page_size == 64 || page_size == 128)) return pl;
+  if (num_pages * B * Hkv * page_size >= (int64_t)INT32_MAX || B * Hkv >= INT32_MAX / 4 || T > 4096 ||
+      ctx_len >= (int64_t)INT32_MAX / 2)
+    return pl;
+  pl.G = (int)G;
+  pl.t_per_tile = (int)(128 / G);
+  pl.n_tiles = (int)((T * G + 127) / 128);
+  pl.n_ctx_chunks = (int)((ctx_len + attn::kChunk - 1) / attn::kChunk);
+  pl.n_chunks = pl.n_ctx_chunks + (int)((T + attn::kChunk - 1) / attn::kChunk);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = sm_count(dev >= 0 && dev < kMaxDevices ? dev : 0);
+  const int64_t units = B * Hkv;
+  int splits = 1;
+  if (units * 4 < (int64_t)sms * 3) {  // fewer units than ~3/4 of the SMs: split the keys
+    splits = (int)(sms / (units > 0 ? units : 1));
+    if (splits > pl.n_chunks) splits = pl.n_chunks;
+    if (splits < 1) splits = 1;
+  }
+  pl.chunks_per_split = (pl.n_chunks + splits - 1) / splits;
+  pl.splits = (pl.n_chunks + pl.chunks_per_split - 1) / pl.chunks_per_split;  // no empty split
+  if (pl.splits > 1) {
+    const size_t slots = (size_t)units * pl.splits * 256;
+    pl.ws_bytes = align256(slots * attn::kD * 4) + align256(slots * 2 * 4);
+  }
+  pl.eligible = true;
+  return pl;
+}
+
+int make_map(CUtensorMap* map, const void* base, int dtype, int rank, const uint64_t* dims, const uint64_t* strides,
+             const uint32_t* box) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(MTP_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t d[5], s[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i < rank - 1) s[i] = strides[i];
+  }
+  const CUtensorMapDataType t =
+      dtype == MTP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, t, (cuuint32_t)rank, const_cast<void*>(base), d, s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTP_ERR_CUDA, "cuTensorMapEncodeTiled (rank %d) failed (%d)", rank, (int)r);
+  return MTP_OK;
+}
+
+int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pages, const void* v_pages,
+                             const int32_t* page_table, int64_t table_stride, int64_t ctx_len, const void* tree_k,
+                             const void* tree_v, const float* tree_mask, void* out, int dtype, int64_t B, int64_t T,
+                             int64_t Hq, int64_t Hkv, int64_t num_pages, int64_t page_size, float scale,
+                             void* workspace, cudaStream_t s) {
+  const uint64_t D = attn::kD, E = 2;
+  CUtensorMap tq, tk, tv, ttk, ttv;
+  {
+    const uint64_t dims[4] = {D, (uint64_t)Hq, (uint64_t)T, (uint64_t)B};
+    const uint64_t str[3] = {D * E, (uint64_t)Hq * D * E, (uint64_t)T * Hq * D * E};
+    const uint32_t box[4] = {64, (uint32_t)pl.G, (uint32_t)pl.t_per_tile, 1};
+    if (int st = make_map(&tq, q, dtype, 4, dims, str, box)) return st;
+  }
+  {
+    // page pools as [P*B*Hkv*page_size, D]: one (page, b, h) slab = page_size consecutive rows
+    const uint64_t rows = (uint64_t)(num_pages > 0 ? num_pages : 1) * B * Hkv * page_size;
+    const uint64_t dims[2] = {D, rows};
+    const uint64_t str[1] = {D * E};
+    const uint32_t box[2] = {64, (uint32_t)page_size};
+    const void* kp = k_pages ? k_pages : tree_k;  // ctx_len == 0: never read
+    const void* vp = v_pages ? v_pages : tree_v;
+    if (int st = make_map(&tk, kp, dtype, 2, dims, str, box)) return st;
+    if (int st = make_map(&tv, vp, dtype, 2, dims, str, box)) return st;
+  }
+  {
+    const uint64_t dims[3] = {D, (uint64_t)T, (uint64_t)(B * Hkv)};
+    const uint64_t str[2] = {D * E, (uint64_t)T * D * E};
+    const uint32_t box[3] = {64, (uint32_t)attn::kChunk, 1};
+    if (int st = make_map(&ttk, tree_k, dtype, 3, dims, str, box)) return st;
+    if (int st = make_map(&ttv, tree_v, dtype, 3, dims, str, box)) return st;
+  }
+  attn::Params p{};
+  p.page_table = page_table;
+  p.table_stride = table_stride;
+  p.tree_mask = tree_mask;
+  p.out = out;
+  p.B = (int)B;
+  p.T = (int)T;
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.G = pl.G;
+  p.ps = (int)page_size;
+  p.num_pages = (int)num_pages;
+  p.ctx_len = (int)ctx_len;
+  p.n_ctx_chunks = pl.n_ctx_chunks;
+  p.n_chunks = pl.n_chunks;
+  p.splits = pl.splits;
+  p.chunks_per_split = pl.chunks_per_split;
+  p.n_tiles = pl.n_tiles;
+  p.t_per_tile = pl.t_per_tile;
+  p.out_dtype = dtype;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  if (pl.splits > 1) {
+    const size_t slots = (size_t)B * Hkv * pl.splits * 256;
+    p.part_o = static_cast<float*>(workspace);
+    p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(slots * attn::kD * 4));
+  }
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  const int grid = (int)(B * Hkv * pl.splits);
+  if (dtype == MTP_DTYPE_BF16) {
+    static bool attr[kMaxDevices] = {false};
+    if (!attr[dev]) {
+      MTP_CUDA_TRY(cudaFuncSetAttribute(attn::tree_attention_tc_kernel<1>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes));
+      attr[dev] = true;
+    }
+    attn::tree_attention_tc_kernel<1><<<grid, attn::kThreads, attn::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
+  } else {
+    static bool attr[kMaxDevices] = {false};
+    if (!attr[dev]) {
+      MTP_CUDA_TRY(cudaFuncSetAttribute(attn::tree_attention_tc_kernel<0>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes));
+      attr[dev] = true;
+    }
+    attn::tree_attention_tc_kernel<0><<<grid, attn::kThreads, attn::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
+  }
+  MTP_LAUNCH_CHECK();
+  if (pl.splits > 1) {
+    const int64_t warps = B * Hkv * pl.n_tiles * 128;
+    attn::attn_merge_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(p);
+    MTP_LAUNCH_CHECK();
+  }
+  return MTP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
                                           int64_t ctx_len) {
-  (void)B, (void)T, (void)Hq, (void)Hkv, (void)D, (void)ctx_len;
-  return 256;
+  // page_size 16 / bf16 give the same plan as every other eligible case of these sizes
+  const TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, 16, 1, MTP_DTYPE_BF16);
+  return pl.ws_bytes;
 }
 
 int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_pages, const int32_t* page_table,
@@ -429,7 +587,6 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
                              const float* tree_mask, void* out, int dtype, int64_t B, int64_t T, int64_t Hq,
                              int64_t Hkv, int64_t D, int64_t num_pages, int64_t page_size, float scale,
                              void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace, (void)workspace_bytes;
   if (B < 0 || T < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || ctx_len < 0 || page_size <= 0 || num_pages < 0)
     return fail(MTP_ERR_SHAPE, "bad tree attention sizes");
   if (Hq % Hkv != 0) return fail(MTP_ERR_SHAPE, "Hq=%lld not a multiple of Hkv=%lld", (long long)Hq, (long long)Hkv);
@@ -438,6 +595,16 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
   if (B * T == 0) return MTP_OK;
   if (!q || !out || !tree_k || !tree_v || !tree_mask || (ctx_len > 0 && (!k_pages || !v_pages || !page_table)))
     return fail(MTP_ERR_ARG, "null tensor pointer");
+  const TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype);
+  const bool aligned = aligned16(q) && aligned16(out) && aligned16(tree_k) && aligned16(tree_v) &&
+                       (ctx_len == 0 || (aligned16(k_pages) && aligned16(v_pages)));
+  if (pl.eligible && aligned) {
+    if (pl.splits > 1 && (!workspace || workspace_bytes < pl.ws_bytes))
+      return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", pl.ws_bytes);
+    return launch_tree_attention_tc(pl, q, k_pages, v_pages, page_table, table_stride, ctx_len, tree_k, tree_v,
+                                    tree_mask, out, dtype, B, T, Hq, Hkv, num_pages, page_size, scale, workspace,
+                                    as_stream(stream));
+  }
   AttnArgs a{};
   a.kind = ATTN_TREE_PAGED;
   a.dtype = dtype;

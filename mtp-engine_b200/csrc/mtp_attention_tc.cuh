@@ -1,0 +1,440 @@
+// mtp_attention_tc.cuh -- paged tree attention with grouped-query heads on
+// the sm_100a tensor cores (tcgen05 + TMEM), the composite of the reference's
+// fused_paged_attention (page-table gather, mtp_kernels.py:495-554) and
+// fused_tree_attention (masked keys, mtp_kernels.py:560-613).
+//
+// Work unit = one (sequence b, KV head). Its query rows are every tree node t
+// times the G = Hq/Hkv query heads that share the KV head: up to 256 rows,
+// held as two 128-row tiles (row r = t_local*G + g) for the whole kernel, so
+// each K/V byte is read from HBM once per unit and feeds 256 query rows.
+//
+// 320 threads, one CTA per SM:
+//   warp 0      TMA producer: Q once (4-D map over [B,T,Hq,D]); then per
+//               128-key chunk the K and V slabs -- context chunks gather
+//               128/page_size pages of the PagedKVCache pool
+//               [P,B,Hkv,page_size,D] (each (page,b,h) slab is contiguous),
+//               the tree chunk reads [B,Hkv,T,D] -- into a 3-deep ring of
+//               32 KB buffers, 128-byte swizzled.
+//   warp 1      TMEM allocator + tcgen05.mma issuer:
+//               S_t = Q_t K^T (M128 N128 K128) and O_t += P_t V
+//               (M128 N128 K128, V read MN-major), accumulators in TMEM
+//               (S0, S1, O0, O1 = 4 x 128 columns), ordered
+//               S0 S1 | PV0 S0' PV1 S1' | ... so one tile's softmax overlaps
+//               the other tile's MMAs.
+//   warps 2-5   softmax for tile 0, warps 6-9 for tile 1: one query row per
+//               thread; tcgen05.ld of the scores, mask (context length, or
+//               the tree ancestor mask), running max in the log2 domain with
+//               lazy rescaling (O in TMEM is rescaled only when the max
+//               grows by more than 2^8), exp2, P written to shared memory in
+//               the UMMA K-major swizzled layout.
+// Long contexts with few units are split over CTAs (flash-decoding); the
+// partial (O, max, sum) triples are merged by attn_merge_kernel.
+// Every wait is bounded (mbar_wait).  No clusters, no TMA multicast.
+#pragma once
+
+#include "mtp_common.cuh"
+
+namespace mtp {
+namespace attn {
+
+constexpr int kThreads = 320;
+constexpr int kD = 128;
+constexpr int kChunk = 128;                      // keys per chunk
+constexpr int kHalfBytes = 128 * 128;            // 128 rows x 128 bytes (64 bf16 of D)
+constexpr int kTileBytes = 2 * kHalfBytes;       // 128 rows x D=128 bf16
+constexpr int kNumBuf = 3;                       // K/V ring depth (32 KB each)
+constexpr int kSmemBytes = 2 * kTileBytes /*Q*/ + kNumBuf * kTileBytes /*K,V*/ + 2 * kTileBytes /*P*/ + 256 + 1024;
+constexpr float kRescaleThreshold = 8.0f;        // log2 units: rescale O only when the max grows by > 2^8
+
+struct Params {
+  const int32_t* page_table;
+  int64_t table_stride;
+  const float* tree_mask;  // [T, T]
+  void* out;               // [B, T, Hq, D]
+  float* part_o;           // [units, splits, 256, D]   (splits > 1)
+  float* part_ml;          // [units, splits, 256, 2]   (max, sum)
+  int B, T, Hq, Hkv, G, ps, num_pages, ctx_len;
+  int n_ctx_chunks, n_chunks, splits, chunks_per_split, n_tiles, t_per_tile;
+  int out_dtype;
+  float scale_log2;  // softmax scale * log2(e)
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi, int dtype) {
+  if (dtype == MTP_DTYPE_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// AB_FMT: 1 = bf16, 0 = f16 (q/k/v dtype)
+template <int AB_FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+    tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmTK,
+                             const __grid_constant__ CUtensorMap tmTV, Params p) {
+  constexpr uint32_t IDESC_S = make_idesc(AB_FMT, 128, kChunk);          // Q (K-major) x K (K-major)
+  constexpr uint32_t IDESC_PV = make_idesc(AB_FMT, 128, kD, 0u, 1u);    // P (K-major) x V (MN-major)
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                  // 2 tiles x 32 KB
+  uint8_t* sBuf = sQ + 2 * kTileBytes;                 // kNumBuf x 32 KB
+  uint8_t* sP = sBuf + kNumBuf * kTileBytes;           // 2 tiles x 32 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* buf_full = bars + 1;
+  uint64_t* buf_empty = buf_full + kNumBuf;
+  uint64_t* s_full = buf_empty + kNumBuf;  // [2]
+  uint64_t* p_full = s_full + 2;           // [2]
+  uint64_t* pv_done = p_full + 2;          // [2]
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int unit = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
+  const int b = unit / p.Hkv, kvh = unit % p.Hkv;
+  const int c0 = split * p.chunks_per_split;
+  const int c1 = min(p.n_chunks, c0 + p.chunks_per_split);
+  const int n_iter = c1 - c0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kNumBuf; ++i) {
+      mbar_init(&buf_full[i], 1);
+      mbar_init(&buf_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&pv_done[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (n_iter > 0 && warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmTK);
+      tma_prefetch_desc(&tmTV);
+      mbar_expect_tx(q_full, p.n_tiles * kTileBytes);
+      for (int t = 0; t < p.n_tiles; ++t)
+        for (int h = 0; h < 2; ++h)
+          tma_load_4d(sQ + t * kTileBytes + h * kHalfBytes, &tmQ, h * 64, kvh * p.G, t * p.t_per_tile, b, q_full);
+      const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
+      const int pages_per_chunk = kChunk / p.ps;
+      int item = 0;
+      bool ok = true;
+      for (int c = c0; c < c1 && ok; ++c) {
+        for (int kv = 0; kv < 2; ++kv, ++item) {
+          const int buf = item % kNumBuf;
+          if (!mbar_wait(&buf_empty[buf], ((item / kNumBuf) & 1) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&buf_full[buf], kTileBytes);
+          uint8_t* dst = sBuf + buf * kTileBytes;
+          if (c < p.n_ctx_chunks) {
+            const CUtensorMap* map = kv ? &tmV : &tmK;
+            const int tok0 = c * kChunk;
+            int first = table[tok0];
+            if (first < 0 || first >= p.num_pages) {
+              record_error(MTP_ERR_DEVICE);
+              first = 0;
+            }
+            for (int i = 0; i < pages_per_chunk; ++i) {
+              const int tok = tok0 + i * p.ps;
+              int page = first;
+              if (tok < p.ctx_len) {
+                page = table[tok];
+                if (page < 0 || page >= p.num_pages) {
+                  record_error(MTP_ERR_DEVICE);
+                  page = 0;
+                }
+                if (kv == 0) {  // a page's tokens must all map to that page
+                  for (int s = 1; s < p.ps && tok + s < p.ctx_len; ++s)
+                    if (table[tok + s] != page) record_error(MTP_ERR_DEVICE);
+                }
+              }
+              const int row = ((page * p.B + b) * p.Hkv + kvh) * p.ps;
+              for (int h = 0; h < 2; ++h)
+                tma_load_2d(dst + h * kHalfBytes + i * p.ps * 128, map, h * 64, row, &buf_full[buf]);
+            }
+          } else {
+            const CUtensorMap* map = kv ? &tmTV : &tmTK;
+            const int tc = c - p.n_ctx_chunks;
+            for (int h = 0; h < 2; ++h)
+              tma_load_3d(dst + h * kHalfBytes, map, h * 64, tc * kChunk, b * p.Hkv + kvh, &buf_full[buf]);
+          }
+        }
+      }
+    }
+  } else if (n_iter > 0 && warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      auto wait_item = [&](int item) -> bool {
+        return mbar_wait(&buf_full[item % kNumBuf], (item / kNumBuf) & 1, abort_flag);
+      };
+      auto issue_s = [&](int t, int buf) {
+        const uint32_t d = tmem_base + (uint32_t)(t * 128);
+        const uint32_t qa = smem_u32(sQ + t * kTileBytes), ka = smem_u32(sBuf + buf * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
+          umma_f16(d, sw128_kmajor_desc(qa + off), sw128_kmajor_desc(ka + off), IDESC_S, k > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int buf, bool acc) {
+        const uint32_t d = tmem_base + (uint32_t)(256 + t * 128);
+        const uint32_t pa = smem_u32(sP + t * kTileBytes), va = smem_u32(sBuf + buf * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // 16 keys per MMA
+          const uint32_t aoff = (k >> 2) * kHalfBytes + (k & 3) * 32;
+          const uint32_t boff = k * 16 * 128;
+          umma_f16(d, sw128_kmajor_desc(pa + aoff), sw128_mnmajor_desc(va + boff, kHalfBytes), IDESC_PV,
+                   (acc || k > 0) ? 1u : 0u);
+        }
+      };
+      if (ok && (ok = wait_item(0))) {
+        tc_fence_after();
+        for (int t = 0; t < p.n_tiles; ++t) {
+          issue_s(t, 0);
+          umma_commit(&s_full[t]);
+        }
+        umma_commit(&buf_empty[0]);
+      }
+      for (int i = 0; i < n_iter && ok; ++i) {
+        const int kitem = 2 * i, vitem = 2 * i + 1, knext = 2 * i + 2;
+        for (int t = 0; t < p.n_tiles && ok; ++t) {
+          if (!(ok = mbar_wait(&p_full[t], i & 1, abort_flag))) break;
+          tc_fence_after();
+          if (t == 0) {
+            if (!(ok = wait_item(vitem))) break;
+            tc_fence_after();
+          }
+          issue_pv(t, vitem % kNumBuf, i > 0);
+          umma_commit(&pv_done[t]);
+          if (t == p.n_tiles - 1) umma_commit(&buf_empty[vitem % kNumBuf]);
+          if (i + 1 < n_iter) {
+            if (t == 0) {
+              if (!(ok = wait_item(knext))) break;
+              tc_fence_after();
+            }
+            issue_s(t, knext % kNumBuf);
+            umma_commit(&s_full[t]);
+            if (t == p.n_tiles - 1) umma_commit(&buf_empty[knext % kNumBuf]);
+          }
+        }
+        (void)kitem;
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, abort_flag, /*honour_abort=*/false);
+    }
+  } else if (n_iter > 0 && warp >= 2 && (warp - 2) / 4 < p.n_tiles) {
+    // ---------------------------------------------------------------- softmax
+    const int t = (warp - 2) / 4;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // row within the tile == TMEM lane
+    const int t_node = t * p.t_per_tile + r / p.G;
+    const int g = r % p.G;
+    const bool row_ok = t_node < p.T;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t s_addr = tmem_base + lane_off + (uint32_t)(t * 128);
+    const uint32_t o_addr = tmem_base + lane_off + (uint32_t)(256 + t * 128);
+    const uint32_t p_base = smem_u32(sP + t * kTileBytes) + (uint32_t)r * 128;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n_iter; ++i) {
+      const int c = c0 + i;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], i & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[128];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) tmem_ld32(s_addr + j * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * j]));
+      tmem_wait_ld();
+      float mx = -INFINITY;
+      if (c < p.n_ctx_chunks) {
+        const int valid = p.ctx_len - c * kChunk;  // keys [0, valid) of this chunk are context tokens
+#pragma unroll
+        for (int j = 0; j < 128; ++j) {
+          const float x = (j < valid) ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
+          s[j] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      } else {
+        const int m0 = (c - p.n_ctx_chunks) * kChunk;
+        const float* mrow = p.tree_mask + (int64_t)(row_ok ? t_node : 0) * p.T;
+#pragma unroll
+        for (int j = 0; j < 128; ++j) {
+          const int m = m0 + j;
+          const bool keep = row_ok && m < p.T && __ldg(mrow + m) > 0.5f;
+          const float x = keep ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
+          s[j] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      if (i > 0) {
+        // P buffer and O may be touched only after the previous PV completed
+        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[t], (i - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const bool need = m_new > m_run + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2(m_run - m_new) : 1.0f;
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + j * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+            tmem_st32(o_addr + j * 32, o);
+          }
+          tmem_wait_st();
+          if (need) {
+            l_run *= alpha;
+            m_run = m_new;
+          }
+        }
+      } else {
+        m_run = m_new;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      float lsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 128; j += 8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float a = ex2(__uint_as_float(s[j + 2 * k]) - m_use);
+          const float bb = ex2(__uint_as_float(s[j + 2 * k + 1]) - m_use);
+          lsum += a + bb;
+          w[k] = pack_bf16(a, bb, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
+        }
+        const int cidx = j >> 3;                  // 16-byte chunk 0..15 of the row
+        const uint32_t half = (uint32_t)(cidx >> 3) * kHalfBytes;
+        const uint32_t chunk = (uint32_t)((cidx & 7) ^ (r & 7)) << 4;
+        sts128(p_base + half + chunk, w[0], w[1], w[2], w[3]);
+      }
+      l_run += lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (n_iter - 1) & 1, abort_flag))) {
+      tc_fence_after();
+      const int row_in_unit = t * 128 + r;
+      if (p.splits == 1) {
+        const float inv = 1.0f / l_run;
+        uint8_t* orow = static_cast<uint8_t*>(p.out) +
+                        ((((int64_t)b * p.T + t_node) * p.Hq + (int64_t)kvh * p.G + g) * kD) * 2;
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + j * 32, o);
+          tmem_wait_ld();
+          if (row_ok) {
+            uint32_t w[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              w[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv, p.out_dtype);
+            uint4* dst = reinterpret_cast<uint4*>(orow + j * 64);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          }
+        }
+      } else {
+        const int64_t slot = ((int64_t)unit * p.splits + split) * 256 + row_in_unit;
+        float* po = p.part_o + slot * kD;
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + j * 32, o);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(po + j * 32);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                                 __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+        }
+        p.part_ml[slot * 2] = m_run;
+        p.part_ml[slot * 2 + 1] = l_run;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// Merge split partials: out = sum_s w_s O_s / sum_s w_s l_s, w_s = 2^(m_s - max m).
+// One warp per (unit, query row); each lane owns 4 of the 128 head dims.
+__global__ void __launch_bounds__(256) attn_merge_kernel(Params p) {
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t units = (int64_t)p.B * p.Hkv;
+  const int rows = p.n_tiles * 128;
+  if (wid >= units * rows) return;
+  const int unit = (int)(wid / rows), row = (int)(wid % rows);
+  const int t = row / 128, r = row % 128;
+  const int t_node = t * p.t_per_tile + r / p.G, g = r % p.G;
+  if (t_node >= p.T) return;
+  const int b = unit / p.Hkv, kvh = unit % p.Hkv;
+  float M = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[(((int64_t)unit * p.splits + s) * 256 + row) * 2]);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, L = 0.f;
+  for (int s = 0; s < p.splits; ++s) {
+    const int64_t slot = ((int64_t)unit * p.splits + s) * 256 + row;
+    const float ms = p.part_ml[slot * 2];
+    const float w = (ms == -INFINITY) ? 0.f : ex2(ms - M);
+    L += w * p.part_ml[slot * 2 + 1];
+    const float4 v = reinterpret_cast<const float4*>(p.part_o + slot * kD)[lane];
+    acc[0] += w * v.x;
+    acc[1] += w * v.y;
+    acc[2] += w * v.z;
+    acc[3] += w * v.w;
+  }
+  const float inv = 1.0f / L;
+  uint8_t* orow = static_cast<uint8_t*>(p.out) + ((((int64_t)b * p.T + t_node) * p.Hq + (int64_t)kvh * p.G + g) * kD) * 2;
+  uint2 w2 = make_uint2(pack_bf16(acc[0] * inv, acc[1] * inv, p.out_dtype), pack_bf16(acc[2] * inv, acc[3] * inv, p.out_dtype));
+  reinterpret_cast<uint2*>(orow)[lane] = w2;
+}
+
+}  // namespace attn
+}  // namespace mtp
