@@ -13,20 +13,22 @@
 //               128-key chunk the K and V slabs -- context chunks gather
 //               128/page_size pages of the PagedKVCache pool
 //               [P,B,Hkv,page_size,D] (each (page,b,h) slab is contiguous),
-//               the tree chunk reads [B,Hkv,T,D] -- into a 3-deep ring of
-//               32 KB buffers, 128-byte swizzled.
+//               the tree chunk reads [B,Hkv,T,D] -- into a 5-deep ring of
+//               32 KB buffers, 128-byte swizzled.  Page-table reads are spread
+//               over the warp's lanes, one page per lane.
 //   warp 1      TMEM allocator + tcgen05.mma issuer:
 //               S_t = Q_t K^T (M128 N128 K128) and O_t += P_t V
-//               (M128 N128 K128, V read MN-major), accumulators in TMEM
-//               (S0, S1, O0, O1 = 4 x 128 columns), ordered
+//               (M128 N128 K128, P read from TMEM, V MN-major from shared
+//               memory), accumulators in TMEM (S0, S1, O0, O1 = 4 x 128
+//               columns; P_t overwrites the first 64 columns of S_t), ordered
 //               S0 S1 | PV0 S0' PV1 S1' | ... so one tile's softmax overlaps
 //               the other tile's MMAs.
 //   warps 2-5   softmax for tile 0, warps 6-9 for tile 1: one query row per
 //               thread; tcgen05.ld of the scores, mask (context length, or
 //               the tree ancestor mask), running max in the log2 domain with
 //               lazy rescaling (O in TMEM is rescaled only when the max
-//               grows by more than 2^8), exp2, P written to shared memory in
-//               the UMMA K-major swizzled layout.
+//               grows by more than 2^8), exp2, P packed to bf16 pairs and
+//               stored back into TMEM with tcgen05.st.
 // Long contexts with few units are split over CTAs (flash-decoding); the
 // partial (O, max, sum) triples are merged by attn_merge_kernel.
 // Every wait is bounded (mbar_wait).  No clusters, no TMA multicast.
@@ -42,8 +44,8 @@ constexpr int kD = 128;
 constexpr int kChunk = 128;                      // keys per chunk
 constexpr int kHalfBytes = 128 * 128;            // 128 rows x 128 bytes (64 bf16 of D)
 constexpr int kTileBytes = 2 * kHalfBytes;       // 128 rows x D=128 bf16
-constexpr int kNumBuf = 3;                       // K/V ring depth (32 KB each)
-constexpr int kSmemBytes = 2 * kTileBytes /*Q*/ + kNumBuf * kTileBytes /*K,V*/ + 2 * kTileBytes /*P*/ + 256 + 1024;
+constexpr int kNumBuf = 5;                       // K/V ring depth (32 KB each)
+constexpr int kSmemBytes = 2 * kTileBytes /*Q*/ + kNumBuf * kTileBytes /*K,V*/ + 256 + 1024;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units: rescale O only when the max grows by > 2^8
 
 struct Params {
@@ -63,10 +65,6 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi, int dtype) {
@@ -91,8 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                  // 2 tiles x 32 KB
   uint8_t* sBuf = sQ + 2 * kTileBytes;                 // kNumBuf x 32 KB
-  uint8_t* sP = sBuf + kNumBuf * kTileBytes;           // 2 tiles x 32 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sBuf + kNumBuf * kTileBytes);
   uint64_t* q_full = bars;
   uint64_t* buf_full = bars + 1;
   uint64_t* buf_empty = buf_full + kNumBuf;
@@ -135,7 +132,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (n_iter > 0 && warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- TMA producer (whole warp)
+    // lane i < pages_per_chunk owns page slot i of a context chunk: it reads
+    // and checks that page's table entries and issues that slab's loads, so
+    // the page-table reads of a chunk overlap; the next chunk's page ids are
+    // fetched before waiting for a free buffer.
+    const int ppc = kChunk / p.ps;
+    const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -146,51 +149,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < p.n_tiles; ++t)
         for (int h = 0; h < 2; ++h)
           tma_load_4d(sQ + t * kTileBytes + h * kHalfBytes, &tmQ, h * 64, kvh * p.G, t * p.t_per_tile, b, q_full);
-      const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
-      const int pages_per_chunk = kChunk / p.ps;
-      int item = 0;
-      bool ok = true;
-      for (int c = c0; c < c1 && ok; ++c) {
-        for (int kv = 0; kv < 2; ++kv, ++item) {
-          const int buf = item % kNumBuf;
-          if (!mbar_wait(&buf_empty[buf], ((item / kNumBuf) & 1) ^ 1u, abort_flag)) {
-            ok = false;
-            break;
+    }
+    auto page_of = [&](int c) -> int {
+      int pg = 0;
+      if (c < p.n_ctx_chunks && lane < ppc) {
+        const int tok = c * kChunk + lane * p.ps;
+        if (tok < p.ctx_len) {
+          pg = table[tok];
+          bool bad = pg < 0 || pg >= p.num_pages;
+          if (!bad)  // every token of a page must map to that page
+            for (int s = 1; s < p.ps && tok + s < p.ctx_len; ++s) bad |= (table[tok + s] != pg);
+          if (bad) {
+            record_error(MTP_ERR_DEVICE);
+            if (pg < 0 || pg >= p.num_pages) pg = 0;
           }
-          mbar_expect_tx(&buf_full[buf], kTileBytes);
-          uint8_t* dst = sBuf + buf * kTileBytes;
-          if (c < p.n_ctx_chunks) {
+        } else {
+          pg = -1;  // slot past the context: reload a valid page, its keys are masked
+        }
+      }
+      const int first = __shfl_sync(0xffffffffu, pg, 0);  // slot 0 of a context chunk is always valid
+      return pg < 0 ? first : pg;
+    };
+    int pg_next = page_of(c0);
+    int item = 0;
+    bool ok = true;
+    for (int c = c0; c < c1 && ok; ++c) {
+      const int pg = pg_next;
+      if (c + 1 < c1) pg_next = page_of(c + 1);
+      for (int kv = 0; kv < 2; ++kv, ++item) {
+        const int buf = item % kNumBuf;
+        bool got = true;
+        if (lane == 0) {
+          got = mbar_wait(&buf_empty[buf], ((item / kNumBuf) & 1) ^ 1u, abort_flag);
+          if (got) mbar_expect_tx(&buf_full[buf], kTileBytes);
+        }
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        uint8_t* dst = sBuf + buf * kTileBytes;
+        if (c < p.n_ctx_chunks) {
+          if (lane < ppc) {
             const CUtensorMap* map = kv ? &tmV : &tmK;
-            const int tok0 = c * kChunk;
-            int first = table[tok0];
-            if (first < 0 || first >= p.num_pages) {
-              record_error(MTP_ERR_DEVICE);
-              first = 0;
-            }
-            for (int i = 0; i < pages_per_chunk; ++i) {
-              const int tok = tok0 + i * p.ps;
-              int page = first;
-              if (tok < p.ctx_len) {
-                page = table[tok];
-                if (page < 0 || page >= p.num_pages) {
-                  record_error(MTP_ERR_DEVICE);
-                  page = 0;
-                }
-                if (kv == 0) {  // a page's tokens must all map to that page
-                  for (int s = 1; s < p.ps && tok + s < p.ctx_len; ++s)
-                    if (table[tok + s] != page) record_error(MTP_ERR_DEVICE);
-                }
-              }
-              const int row = ((page * p.B + b) * p.Hkv + kvh) * p.ps;
-              for (int h = 0; h < 2; ++h)
-                tma_load_2d(dst + h * kHalfBytes + i * p.ps * 128, map, h * 64, row, &buf_full[buf]);
-            }
-          } else {
-            const CUtensorMap* map = kv ? &tmTV : &tmTK;
-            const int tc = c - p.n_ctx_chunks;
+            const int row = ((pg * p.B + b) * p.Hkv + kvh) * p.ps;
             for (int h = 0; h < 2; ++h)
-              tma_load_3d(dst + h * kHalfBytes, map, h * 64, tc * kChunk, b * p.Hkv + kvh, &buf_full[buf]);
+              tma_load_2d(dst + h * kHalfBytes + lane * p.ps * 128, map, h * 64, row, &buf_full[buf]);
           }
+        } else if (lane == 0) {
+          const CUtensorMap* map = kv ? &tmTV : &tmTK;
+          const int tc = c - p.n_ctx_chunks;
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(dst + h * kHalfBytes, map, h * 64, tc * kChunk, b * p.Hkv + kvh, &buf_full[buf]);
         }
       }
     }
@@ -212,14 +222,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto issue_pv = [&](int t, int buf, bool acc) {
         const uint32_t d = tmem_base + (uint32_t)(256 + t * 128);
-        const uint32_t pa = smem_u32(sP + t * kTileBytes), va = smem_u32(sBuf + buf * kTileBytes);
+        const uint32_t pa = tmem_base + (uint32_t)(t * 128);  // P (bf16 pairs) over S_t's first 64 columns
+        const uint32_t va = smem_u32(sBuf + buf * kTileBytes);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // 16 keys per MMA
-          const uint32_t aoff = (k >> 2) * kHalfBytes + (k & 3) * 32;
-          const uint32_t boff = k * 16 * 128;
-          umma_f16(d, sw128_kmajor_desc(pa + aoff), sw128_mnmajor_desc(va + boff, kHalfBytes), IDESC_PV,
-                   (acc || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < 8; ++k)  // 16 keys per MMA: 8 TMEM columns of P, 16 rows of V
+          umma_f16_ts(d, pa + k * 8, sw128_mnmajor_desc(va + k * 16 * 128, kHalfBytes), IDESC_PV,
+                      (acc || k > 0) ? 1u : 0u);
       };
       if (ok && (ok = wait_item(0))) {
         tc_fence_after();
@@ -267,7 +275,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t s_addr = tmem_base + lane_off + (uint32_t)(t * 128);
     const uint32_t o_addr = tmem_base + lane_off + (uint32_t)(256 + t * 128);
-    const uint32_t p_base = smem_u32(sP + t * kTileBytes) + (uint32_t)r * 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int i = 0; i < n_iter; ++i) {
@@ -334,22 +341,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       float lsum = 0.f;
 #pragma unroll
-      for (int j = 0; j < 128; j += 8) {
-        uint32_t w[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float a = ex2(__uint_as_float(s[j + 2 * k]) - m_use);
-          const float bb = ex2(__uint_as_float(s[j + 2 * k + 1]) - m_use);
-          lsum += a + bb;
-          w[k] = pack_bf16(a, bb, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
-        }
-        const int cidx = j >> 3;                  // 16-byte chunk 0..15 of the row
-        const uint32_t half = (uint32_t)(cidx >> 3) * kHalfBytes;
-        const uint32_t chunk = (uint32_t)((cidx & 7) ^ (r & 7)) << 4;
-        sts128(p_base + half + chunk, w[0], w[1], w[2], w[3]);
+      for (int j = 0; j < 64; ++j) {  // packed in place: s[j] is free once s[2j], s[2j+1] are read
+        const float a = ex2(__uint_as_float(s[2 * j]) - m_use);
+        const float bb = ex2(__uint_as_float(s[2 * j + 1]) - m_use);
+        lsum += a + bb;
+        s[j] = pack_bf16(a, bb, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
       }
       l_run += lsum;
-      fence_proxy_async_smem();
+      // P replaces the first 64 columns of S_t: the A operand of O_t += P V
+      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
