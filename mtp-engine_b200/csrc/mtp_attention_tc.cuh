@@ -284,34 +284,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t s[128];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) tmem_ld32(s_addr + j * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * j]));
-      tmem_wait_ld();
+      // pass 1: row max of the scaled, masked scores (32 TMEM columns at a time)
+      const bool is_ctx = c < p.n_ctx_chunks;
+      const int valid = p.ctx_len - c * kChunk;  // context chunk: keys [0, valid) are real tokens
+      const int m0 = (c - p.n_ctx_chunks) * kChunk;
+      const float* mrow = p.tree_mask + (int64_t)(row_ok ? t_node : 0) * p.T;
+      auto xval = [&](uint32_t raw, int j) -> float {
+        bool keep;
+        if (is_ctx) keep = j < valid;
+        else keep = row_ok && m0 + j < p.T && __ldg(mrow + m0 + j) > 0.5f;
+        return keep ? __uint_as_float(raw) * p.scale_log2 : -INFINITY;
+      };
       float mx = -INFINITY;
-      if (c < p.n_ctx_chunks) {
-        const int valid = p.ctx_len - c * kChunk;  // keys [0, valid) of this chunk are context tokens
+#pragma unroll 1
+      for (int j = 0; j < 4; j += 2) {
+        uint32_t a[32], a2[32];
+        tmem_ld32(s_addr + j * 32, a);
+        tmem_ld32(s_addr + (j + 1) * 32, a2);
+        tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const float x = (j < valid) ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
-          s[j] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
-      } else {
-        const int m0 = (c - p.n_ctx_chunks) * kChunk;
-        const float* mrow = p.tree_mask + (int64_t)(row_ok ? t_node : 0) * p.T;
-#pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const int m = m0 + j;
-          const bool keep = row_ok && m < p.T && __ldg(mrow + m) > 0.5f;
-          const float x = keep ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
-          s[j] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
+        for (int k = 0; k < 32; ++k) mx = fmaxf(mx, fmaxf(xval(a[k], j * 32 + k), xval(a2[k], j * 32 + 32 + k)));
       }
       const float m_new = fmaxf(m_run, mx);
       if (i > 0) {
-        // P buffer and O may be touched only after the previous PV completed
+        // P and O may be touched only after the previous PV completed
         if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[t], (i - 1) & 1, abort_flag))) {
           ok = false;
           break;
@@ -338,19 +334,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         m_run = m_new;
       }
+      // pass 2: P = 2^(x - m) as bf16 pairs; the 16 packed columns of block j
+      // overwrite S columns 16j..16j+15, all of which were read in blocks < j
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       float lsum = 0.f;
+#pragma unroll 1
+      for (int j = 0; j < 4; ++j) {
+        uint32_t a[32], pk[16];
+        tmem_ld32(s_addr + j * 32, a);
+        tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {  // packed in place: s[j] is free once s[2j], s[2j+1] are read
-        const float a = ex2(__uint_as_float(s[2 * j]) - m_use);
-        const float bb = ex2(__uint_as_float(s[2 * j + 1]) - m_use);
-        lsum += a + bb;
-        s[j] = pack_bf16(a, bb, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
+        for (int k = 0; k < 16; ++k) {
+          const float e0 = ex2(xval(a[2 * k], j * 32 + 2 * k) - m_use);
+          const float e1 = ex2(xval(a[2 * k + 1], j * 32 + 2 * k + 1) - m_use);
+          lsum += e0 + e1;
+          pk[k] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
+        }
+        tmem_st16(s_addr + j * 16, pk);
       }
       l_run += lsum;
-      // P replaces the first 64 columns of S_t: the A operand of O_t += P V
-      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
