@@ -249,6 +249,16 @@ const char* mtp_last_error(void) { return g_err; }
 
 uint64_t mtp_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+#ifdef MTP_ATTN_TRACE
+// profiling builds only: copy the attention kernel's cycle stamps to the host
+int mtp_attn_trace_read(unsigned long long* host, int n) {
+  MTP_CUDA_TRY(cudaDeviceSynchronize());
+  const int cap = (int)(sizeof(attn::g_attn_trace) / sizeof(unsigned long long));
+  MTP_CUDA_TRY(cudaMemcpyFromSymbol(host, attn::g_attn_trace, sizeof(unsigned long long) * (n < cap ? n : cap)));
+  return MTP_OK;
+}
+#endif
+
 int mtp_gemm_test(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,
                   int force_simt, void* stream) {
   if (int st = check_dims(M, N, K)) return st;

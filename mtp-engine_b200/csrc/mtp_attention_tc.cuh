@@ -48,6 +48,22 @@ constexpr int kNumBuf = 5;                       // K/V ring depth (32 KB each)
 constexpr int kSmemBytes = 2 * kTileBytes /*Q*/ + kNumBuf * kTileBytes /*K,V*/ + 256 + 1024;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units: rescale O only when the max grows by > 2^8
 
+// Optional cycle stamps of CTA 0 (build with -DMTP_ATTN_TRACE): slot
+// (role, tile, iteration) -> clock64.  Compiled out otherwise.
+#ifdef MTP_ATTN_TRACE
+static __device__ unsigned long long g_attn_trace[8 * 2 * 64];
+#define ATTN_TRACE_IF(cond, k, tile, it)                                         \
+  do {                                                                           \
+    if (blockIdx.x == 0 && (cond) && (it) < 64)                                  \
+      g_attn_trace[(((k) * 2 + (tile)) * 64 + (it))] = clock64();                \
+  } while (0)
+#else
+#define ATTN_TRACE_IF(cond, k, tile, it) \
+  do {                                   \
+  } while (0)
+#endif
+#define ATTN_TRACE(k, tile, it) ATTN_TRACE_IF(r == 0, k, tile, it)
+
 struct Params {
   const int32_t* page_table;
   int64_t table_stride;
@@ -187,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        ATTN_TRACE_IF(lane == 0, 6 + kv, 0, c - c0);
         __syncwarp();
         uint8_t* dst = sBuf + buf * kTileBytes;
         if (c < p.n_ctx_chunks) {
@@ -242,6 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < p.n_tiles && ok; ++t) {
           if (!(ok = mbar_wait(&p_full[t], i & 1, abort_flag))) break;
           tc_fence_after();
+          ATTN_TRACE_IF(true, 4, t, i);
           if (t == 0) {
             if (!(ok = wait_item(vitem))) break;
             tc_fence_after();
@@ -256,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             issue_s(t, knext % kNumBuf);
             umma_commit(&s_full[t]);
+            ATTN_TRACE_IF(true, 5, t, i);
             if (t == p.n_tiles - 1) umma_commit(&buf_empty[knext % kNumBuf]);
           }
         }
@@ -284,26 +303,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      // pass 1: row max of the scaled, masked scores (32 TMEM columns at a time)
-      const bool is_ctx = c < p.n_ctx_chunks;
-      const int valid = p.ctx_len - c * kChunk;  // context chunk: keys [0, valid) are real tokens
-      const int m0 = (c - p.n_ctx_chunks) * kChunk;
-      const float* mrow = p.tree_mask + (int64_t)(row_ok ? t_node : 0) * p.T;
-      auto xval = [&](uint32_t raw, int j) -> float {
-        bool keep;
-        if (is_ctx) keep = j < valid;
-        else keep = row_ok && m0 + j < p.T && __ldg(mrow + m0 + j) > 0.5f;
-        return keep ? __uint_as_float(raw) * p.scale_log2 : -INFINITY;
-      };
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int j = 0; j < 4; j += 2) {
-        uint32_t a[32], a2[32];
-        tmem_ld32(s_addr + j * 32, a);
-        tmem_ld32(s_addr + (j + 1) * 32, a2);
-        tmem_wait_ld();
+      ATTN_TRACE(0, t, i);
+      // the whole 128-column score row in one TMEM round trip
+      uint32_t s[128];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) mx = fmaxf(mx, fmaxf(xval(a[k], j * 32 + k), xval(a2[k], j * 32 + 32 + k)));
+      for (int j = 0; j < 4; ++j) tmem_ld32(s_addr + j * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * j]));
+      tmem_wait_ld();
+      ATTN_TRACE(1, t, i);
+      float mx = -INFINITY;
+      if (c < p.n_ctx_chunks) {
+        const int valid = p.ctx_len - c * kChunk;  // keys [0, valid) of this chunk are context tokens
+#pragma unroll
+        for (int j = 0; j < 128; ++j) {
+          const float x = (j < valid) ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
+          s[j] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      } else {
+        const int m0 = (c - p.n_ctx_chunks) * kChunk;
+        const float* mrow = p.tree_mask + (int64_t)(row_ok ? t_node : 0) * p.T;
+#pragma unroll
+        for (int j = 0; j < 128; ++j) {
+          const int m = m0 + j;
+          const bool keep = row_ok && m < p.T && __ldg(mrow + m) > 0.5f;
+          const float x = keep ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
+          s[j] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
       }
       const float m_new = fmaxf(m_run, mx);
       if (i > 0) {
@@ -313,17 +339,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        ATTN_TRACE(2, t, i);
         const bool need = m_new > m_run + kRescaleThreshold;
         if (__any_sync(0xffffffffu, need)) {
           const float alpha = need ? ex2(m_run - m_new) : 1.0f;
 #pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
-            uint32_t o[32];
-            tmem_ld32(o_addr + j * 32, o);
+          for (int j = 0; j < 8; ++j) {
+            uint32_t o[16];
+            tmem_ld16(o_addr + j * 16, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-            tmem_st32(o_addr + j * 32, o);
+            for (int k = 0; k < 16; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+            tmem_st16(o_addr + j * 16, o);
           }
           tmem_wait_st();
           if (need) {
@@ -334,26 +361,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         m_run = m_new;
       }
-      // pass 2: P = 2^(x - m) as bf16 pairs; the 16 packed columns of block j
-      // overwrite S columns 16j..16j+15, all of which were read in blocks < j
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       float lsum = 0.f;
-#pragma unroll 1
-      for (int j = 0; j < 4; ++j) {
-        uint32_t a[32], pk[16];
-        tmem_ld32(s_addr + j * 32, a);
-        tmem_wait_ld();
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float e0 = ex2(xval(a[2 * k], j * 32 + 2 * k) - m_use);
-          const float e1 = ex2(xval(a[2 * k + 1], j * 32 + 2 * k + 1) - m_use);
-          lsum += e0 + e1;
-          pk[k] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
-        }
-        tmem_st16(s_addr + j * 16, pk);
+      for (int j = 0; j < 64; ++j) {  // packed in place: s[j] is free once s[2j], s[2j+1] are read
+        const float e0 = ex2(__uint_as_float(s[2 * j]) - m_use);
+        const float e1 = ex2(__uint_as_float(s[2 * j + 1]) - m_use);
+        lsum += e0 + e1;
+        s[j] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
       }
       l_run += lsum;
+      // P replaces the first 64 columns of S_t: the A operand of O_t += P V
+      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
       tmem_wait_st();
+      ATTN_TRACE(3, t, i);
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
