@@ -546,6 +546,7 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
   p.n_tiles = pl.n_tiles;
   p.t_per_tile = pl.t_per_tile;
   p.out_dtype = dtype;
+  p.table_vec = (reinterpret_cast<uintptr_t>(page_table) % 16 == 0) && (table_stride % 4 == 0);
   p.scale_log2 = scale * 1.4426950408889634f;
   if (pl.splits > 1) {
     const size_t slots = (size_t)B * Hkv * pl.splits * 256;

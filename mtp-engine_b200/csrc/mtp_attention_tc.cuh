@@ -8,14 +8,13 @@
 // held as two 128-row tiles (row r = t_local*G + g) for the whole kernel, so
 // each K/V byte is read from HBM once per unit and feeds 256 query rows.
 //
-// 320 threads, one CTA per SM:
+// 352 threads, one CTA per SM:
 //   warp 0      TMA producer: Q once (4-D map over [B,T,Hq,D]); then per
 //               128-key chunk the K and V slabs -- context chunks gather
 //               128/page_size pages of the PagedKVCache pool
 //               [P,B,Hkv,page_size,D] (each (page,b,h) slab is contiguous),
 //               the tree chunk reads [B,Hkv,T,D] -- into a 5-deep ring of
-//               32 KB buffers, 128-byte swizzled.  Page-table reads are spread
-//               over the warp's lanes, one page per lane.
+//               32 KB buffers, 128-byte swizzled; one lane per page slab.
 //   warp 1      TMEM allocator + tcgen05.mma issuer:
 //               S_t = Q_t K^T (M128 N128 K128) and O_t += P_t V
 //               (M128 N128 K128, P read from TMEM, V MN-major from shared
@@ -29,6 +28,8 @@
 //               lazy rescaling (O in TMEM is rescaled only when the max
 //               grows by more than 2^8), exp2, P packed to bf16 pairs and
 //               stored back into TMEM with tcgen05.st.
+//   warp 10     page-table reader: checks and stages the page ids of up to
+//               16 chunks ahead of the TMA producer (shared-memory ring).
 // Long contexts with few units are split over CTAs (flash-decoding); the
 // partial (O, max, sum) triples are merged by attn_merge_kernel.
 // Every wait is bounded (mbar_wait).  No clusters, no TMA multicast.
@@ -39,13 +40,16 @@
 namespace mtp {
 namespace attn {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;                    // 11 warps (see the role list above)
 constexpr int kD = 128;
 constexpr int kChunk = 128;                      // keys per chunk
 constexpr int kHalfBytes = 128 * 128;            // 128 rows x 128 bytes (64 bf16 of D)
 constexpr int kTileBytes = 2 * kHalfBytes;       // 128 rows x D=128 bf16
 constexpr int kNumBuf = 5;                       // K/V ring depth (32 KB each)
-constexpr int kSmemBytes = 2 * kTileBytes /*Q*/ + kNumBuf * kTileBytes /*K,V*/ + 256 + 1024;
+constexpr int kIdRing = 16;                      // page-id ring: chunks the table warp may run ahead
+constexpr int kMaxPagesPerChunk = 16;            // page_size >= 8
+constexpr int kSmemBytes = 2 * kTileBytes /*Q*/ + kNumBuf * kTileBytes /*K,V*/ +
+                           kIdRing * kMaxPagesPerChunk * 4 /*page ids*/ + 512 /*barriers*/ + 1024;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units: rescale O only when the max grows by > 2^8
 
 // Optional cycle stamps of CTA 0 (build with -DMTP_ATTN_TRACE): slot
@@ -74,6 +78,7 @@ struct Params {
   int B, T, Hq, Hkv, G, ps, num_pages, ctx_len;
   int n_ctx_chunks, n_chunks, splits, chunks_per_split, n_tiles, t_per_tile;
   int out_dtype;
+  int table_vec;     // page-table rows 16-byte aligned: check pages with int4 loads
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -105,14 +110,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                  // 2 tiles x 32 KB
   uint8_t* sBuf = sQ + 2 * kTileBytes;                 // kNumBuf x 32 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sBuf + kNumBuf * kTileBytes);
+  int* sIds = reinterpret_cast<int*>(sBuf + kNumBuf * kTileBytes);  // [kIdRing][kMaxPagesPerChunk]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sIds + kIdRing * kMaxPagesPerChunk);
   uint64_t* q_full = bars;
   uint64_t* buf_full = bars + 1;
   uint64_t* buf_empty = buf_full + kNumBuf;
   uint64_t* s_full = buf_empty + kNumBuf;  // [2]
   uint64_t* p_full = s_full + 2;           // [2]
   uint64_t* pv_done = p_full + 2;          // [2]
-  uint64_t* drain = pv_done + 2;
+  uint64_t* ids_full = pv_done + 2;        // [kIdRing]
+  uint64_t* ids_empty = ids_full + kIdRing;  // [kIdRing]
+  uint64_t* drain = ids_empty + kIdRing;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -134,6 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_full[t], 128);
       mbar_init(&pv_done[t], 1);
     }
+    for (int i = 0; i < kIdRing; ++i) {
+      mbar_init(&ids_full[i], 1);
+      mbar_init(&ids_empty[i], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -149,12 +161,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (n_iter > 0 && warp == 0) {
     // ---------------------------------------------------------------- TMA producer (whole warp)
-    // lane i < pages_per_chunk owns page slot i of a context chunk: it reads
-    // and checks that page's table entries and issues that slab's loads, so
-    // the page-table reads of a chunk overlap; the next chunk's page ids are
-    // fetched before waiting for a free buffer.
+    // lane i < pages_per_chunk issues the loads of page slot i of a context
+    // chunk; page ids come checked from the table warp through sIds.
     const int ppc = kChunk / p.ps;
-    const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -166,32 +175,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = 0; h < 2; ++h)
           tma_load_4d(sQ + t * kTileBytes + h * kHalfBytes, &tmQ, h * 64, kvh * p.G, t * p.t_per_tile, b, q_full);
     }
-    auto page_of = [&](int c) -> int {
-      int pg = 0;
-      if (c < p.n_ctx_chunks && lane < ppc) {
-        const int tok = c * kChunk + lane * p.ps;
-        if (tok < p.ctx_len) {
-          pg = table[tok];
-          bool bad = pg < 0 || pg >= p.num_pages;
-          if (!bad)  // every token of a page must map to that page
-            for (int s = 1; s < p.ps && tok + s < p.ctx_len; ++s) bad |= (table[tok + s] != pg);
-          if (bad) {
-            record_error(MTP_ERR_DEVICE);
-            if (pg < 0 || pg >= p.num_pages) pg = 0;
-          }
-        } else {
-          pg = -1;  // slot past the context: reload a valid page, its keys are masked
-        }
-      }
-      const int first = __shfl_sync(0xffffffffu, pg, 0);  // slot 0 of a context chunk is always valid
-      return pg < 0 ? first : pg;
-    };
-    int pg_next = page_of(c0);
     int item = 0;
     bool ok = true;
     for (int c = c0; c < c1 && ok; ++c) {
-      const int pg = pg_next;
-      if (c + 1 < c1) pg_next = page_of(c + 1);
+      const bool is_ctx = c < p.n_ctx_chunks;
+      const int slot = (c - c0) % kIdRing;
+      int pg = 0;
+      if (is_ctx) {
+        bool got = true;
+        if (lane == 0) got = mbar_wait(&ids_full[slot], ((c - c0) / kIdRing) & 1, abort_flag);
+        if (!__shfl_sync(0xffffffffu, got, 0)) break;
+        if (lane < ppc) pg = sIds[slot * kMaxPagesPerChunk + lane];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ids_empty[slot]);
+      }
       for (int kv = 0; kv < 2; ++kv, ++item) {
         const int buf = item % kNumBuf;
         bool got = true;
@@ -206,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ATTN_TRACE_IF(lane == 0, 6 + kv, 0, c - c0);
         __syncwarp();
         uint8_t* dst = sBuf + buf * kTileBytes;
-        if (c < p.n_ctx_chunks) {
+        if (is_ctx) {
           if (lane < ppc) {
             const CUtensorMap* map = kv ? &tmV : &tmK;
             const int row = ((pg * p.B + b) * p.Hkv + kvh) * p.ps;
@@ -220,6 +217,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(dst + h * kHalfBytes, map, h * 64, tc * kChunk, b * p.Hkv + kvh, &buf_full[buf]);
         }
       }
+    }
+  } else if (n_iter > 0 && warp == 10) {
+    // ---------------------------------------------------------------- page-table warp
+    // Reads and checks the page ids of up to kIdRing context chunks ahead of
+    // the TMA producer: lane i < pages_per_chunk takes page slot i, checks
+    // that every token of the page maps to the same in-range page (the
+    // reference gathers per token, mtp_kernels.py:520-531; whole-page loads
+    // are only equivalent when the table is page-granular, as PagedKVCache
+    // builds it) and records MTP_ERR_DEVICE otherwise.
+    const int ppc = kChunk / p.ps;
+    const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
+    const int c_end = min(c1, p.n_ctx_chunks);
+    for (int c = c0; c < c_end; ++c) {
+      const int slot = (c - c0) % kIdRing;
+      bool got = true;
+      if (lane == 0) got = mbar_wait(&ids_empty[slot], (((c - c0) / kIdRing) & 1) ^ 1u, abort_flag);
+      if (!__shfl_sync(0xffffffffu, got, 0)) break;
+      int pg = -1;  // slot past the context: reload a valid page, its keys are masked
+      if (lane < ppc) {
+        const int tok = c * kChunk + lane * p.ps;
+        if (tok < p.ctx_len) {
+          pg = table[tok];
+          const int n = min(p.ps, p.ctx_len - tok);
+          bool bad = pg < 0 || pg >= p.num_pages;
+          if (p.table_vec && n == p.ps) {
+            const int4* v = reinterpret_cast<const int4*>(table + tok);
+            for (int s = 0; s < p.ps / 4; ++s) {
+              const int4 e = __ldg(v + s);
+              bad |= (e.x != pg) | (e.y != pg) | (e.z != pg) | (e.w != pg);
+            }
+          } else {
+            for (int s = 1; s < n; ++s) bad |= (table[tok + s] != pg);
+          }
+          if (bad) {
+            record_error(MTP_ERR_DEVICE);
+            if (pg < 0 || pg >= p.num_pages) pg = 0;
+          }
+        }
+      }
+      const int first = __shfl_sync(0xffffffffu, pg, 0);  // slot 0 of a context chunk is always valid
+      if (lane < ppc) sIds[slot * kMaxPagesPerChunk + lane] = pg < 0 ? first : pg;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ids_full[slot]);
     }
   } else if (n_iter > 0 && warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
