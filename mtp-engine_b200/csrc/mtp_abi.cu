@@ -609,7 +609,7 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
   const TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype);
   const bool aligned = aligned16(q) && aligned16(out) && aligned16(tree_k) && aligned16(tree_v) &&
                        (ctx_len == 0 || (aligned16(k_pages) && aligned16(v_pages)));
-  if (pl.eligible && aligned) {
+  if (pl.eligible && aligned && scale > 0.f) {  // the kernel folds a positive scale into exp2
     if (pl.splits > 1 && (!workspace || workspace_bytes < pl.ws_bytes))
       return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", pl.ws_bytes);
     return launch_tree_attention_tc(pl, q, k_pages, v_pages, page_table, table_stride, ctx_len, tree_k, tree_v,

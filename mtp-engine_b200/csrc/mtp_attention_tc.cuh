@@ -350,27 +350,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 4; ++j) tmem_ld32(s_addr + j * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * j]));
       tmem_wait_ld();
       ATTN_TRACE(1, t, i);
-      float mx = -INFINITY;
+      // Row max on the raw scores: the scale is positive (checked on the
+      // host), so max(s)*scale == max(s*scale) and the scale is folded into
+      // the exponent below.  Masked keys become -inf.  Eight independent
+      // partial maxima keep the dependency chains short.
+      uint32_t mw[4];  // keep-bits of the 128 keys of this chunk
       if (c < p.n_ctx_chunks) {
-        const int valid = p.ctx_len - c * kChunk;  // keys [0, valid) of this chunk are context tokens
+        const int valid = p.ctx_len - c * kChunk;  // keys [0, valid) are context tokens
 #pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const float x = (j < valid) ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
-          s[j] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+        for (int w = 0; w < 4; ++w) {
+          const int v = valid - 32 * w;
+          mw[w] = v >= 32 ? 0xffffffffu : (v <= 0 ? 0u : ((1u << v) - 1u));
         }
       } else {
         const int m0 = (c - p.n_ctx_chunks) * kChunk;
         const float* mrow = p.tree_mask + (int64_t)(row_ok ? t_node : 0) * p.T;
-#pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const int m = m0 + j;
-          const bool keep = row_ok && m < p.T && __ldg(mrow + m) > 0.5f;
-          const float x = keep ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
-          s[j] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+#pragma unroll 1
+        for (int w = 0; w < 4; ++w) {
+          uint32_t bits = 0;
+#pragma unroll 8
+          for (int k = 0; k < 32; ++k) {
+            const int m = m0 + 32 * w + k;
+            if (row_ok && m < p.T && __ldg(mrow + m) > 0.5f) bits |= 1u << k;
+          }
+          mw[w] = bits;
         }
       }
+      if ((mw[0] & mw[1] & mw[2] & mw[3]) != 0xffffffffu) {
+#pragma unroll
+        for (int j = 0; j < 128; ++j)
+          if (!((mw[j >> 5] >> (j & 31)) & 1u)) s[j] = 0xff800000u;  // -inf
+      }
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(s[k]);
+#pragma unroll
+      for (int j = 8; j < 128; ++j) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(s[j]));
+      const float mx = p.scale_log2 * fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                            fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      const float mul = p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       if (i > 0) {
         // P and O may be touched only after the previous PV completed
@@ -402,15 +420,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float lsum = 0.f;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < 64; ++j) {  // packed in place: s[j] is free once s[2j], s[2j+1] are read
-        const float e0 = ex2(__uint_as_float(s[2 * j]) - m_use);
-        const float e1 = ex2(__uint_as_float(s[2 * j + 1]) - m_use);
-        lsum += e0 + e1;
+        const float e0 = ex2(fmaf(__uint_as_float(s[2 * j]), mul, -m_use));
+        const float e1 = ex2(fmaf(__uint_as_float(s[2 * j + 1]), mul, -m_use));
+        ls[j & 3] += e0 + e1;
         s[j] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
       }
-      l_run += lsum;
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // P replaces the first 64 columns of S_t: the A operand of O_t += P V
       tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
       tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
