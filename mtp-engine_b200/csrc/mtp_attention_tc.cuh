@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 128);
+      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
       mbar_init(&pv_done[t], 1);
     }
     for (int i = 0; i < kIdRing; ++i) {
@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           issue_pv(t, vitem % kNumBuf, i > 0);
           umma_commit(&pv_done[t]);
+          ATTN_TRACE_IF(true, 2, t, 32 + (i & 31));
           if (t == p.n_tiles - 1) umma_commit(&buf_empty[vitem % kNumBuf]);
           if (i + 1 < n_iter) {
             if (t == 0) {
@@ -435,7 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       ATTN_TRACE(3, t, i);
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     if (ok && __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (n_iter - 1) & 1, abort_flag))) {
       tc_fence_after();
