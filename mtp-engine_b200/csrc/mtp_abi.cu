@@ -138,24 +138,52 @@ int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   return MTP_OK;
 }
 
+// Tile width for a persistent launch: fewest (rounds x (BN + 16)) over the
+// instantiated widths, rounds = ceil(tiles / SMs); the +16 stands for the
+// fixed per-tile cost that favours wider tiles at equal rounds.
+int pick_bn(int64_t M, int64_t N, int sms) {
+  static const int cands[5] = {256, 224, 192, 160, 128};
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int bn : cands) {
+    if (bn > 128 && N <= 128) continue;
+    const int64_t tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + bn - 1) / bn);
+    const int64_t rounds = (tiles + sms - 1) / sms;
+    const int64_t cost = rounds * (bn + 16);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <bool FP8, int FMT>
+int launch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int num_kb,
+                 const GemmEpilogue& ep, cudaStream_t s) {
+  switch (bn) {
+    case 256: return launch_tc_inst<256, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    case 224: return launch_tc_inst<224, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    case 192: return launch_tc_inst<192, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    case 160: return launch_tc_inst<160, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    default: return launch_tc_inst<128, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+  }
+}
+
 // A [M,K] and B [N,K] both K-major, 16-bit (ab_dtype) or E4M3 (fp8).
 int launch_gemm_tc(const void* A, const void* B, int ab_dtype, bool fp8, int64_t M, int64_t N, int64_t K,
                    const GemmEpilogue& ep, cudaStream_t s) {
-  const int bn = N > 128 ? 256 : 128;
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  const int bn = pick_bn(M, N, sm_count(dev));
   CUtensorMap ta, tb;
   if (int st = make_kmajor_map(&ta, A, fp8, ab_dtype, M, K, tc::kBM)) return st;
   if (int st = make_kmajor_map(&tb, B, fp8, ab_dtype, N, K, bn)) return st;
   const int eb = fp8 ? 1 : 2;
   const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
-  if (fp8) {
-    return bn == 256 ? launch_tc_inst<256, true, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s)
-                     : launch_tc_inst<128, true, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s);
-  }
-  if (ab_dtype == MTP_DTYPE_BF16)
-    return bn == 256 ? launch_tc_inst<256, false, 1>(ta, tb, (int)M, (int)N, num_kb, ep, s)
-                     : launch_tc_inst<128, false, 1>(ta, tb, (int)M, (int)N, num_kb, ep, s);
-  return bn == 256 ? launch_tc_inst<256, false, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s)
-                   : launch_tc_inst<128, false, 0>(ta, tb, (int)M, (int)N, num_kb, ep, s);
+  if (fp8) return launch_tc_bn<true, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
+  if (ab_dtype == MTP_DTYPE_BF16) return launch_tc_bn<false, 1>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
+  return launch_tc_bn<false, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
 }
 
 bool tc_eligible(const void* A, const void* B, int a_dt, int b_dt, int64_t M, int64_t N, int64_t K) {
@@ -189,6 +217,24 @@ int launch_rownorm(const void* x, int x_dt, const void* gamma, int g_dt, const f
                    int64_t K, float eps, int mode, float* row_out, void* xo, int xo_dt, cudaStream_t s) {
   if (M == 0) return MTP_OK;
   if (M > INT32_MAX) return fail(MTP_ERR_SHAPE, "too many rows");
+  const bool vec = mode != ROW_PREQUANT && K % 8 == 0 && aligned16(x) && (!xo || aligned16(xo)) &&
+                   (mode != ROW_GAMMA || (g_dt == MTP_DTYPE_F32 && aligned16(gamma) && xo_dt == x_dt)) &&
+                   (mode != ROW_QUANT || xo_dt == MTP_DTYPE_E4M3) &&
+                   (x_dt == MTP_DTYPE_F32 || x_dt == MTP_DTYPE_BF16 || x_dt == MTP_DTYPE_F16);
+  if (vec) {
+    const float* g = static_cast<const float*>(gamma);
+    if (x_dt == MTP_DTYPE_BF16)
+      rownorm_vec_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), g, (int)K,
+                                                                    eps, mode, row_out, xo);
+    else if (x_dt == MTP_DTYPE_F16)
+      rownorm_vec_kernel<__half><<<(unsigned)M, 256, 0, s>>>(static_cast<const __half*>(x), g, (int)K, eps, mode,
+                                                             row_out, xo);
+    else
+      rownorm_vec_kernel<float><<<(unsigned)M, 256, 0, s>>>(static_cast<const float*>(x), g, (int)K, eps, mode,
+                                                            row_out, xo);
+    MTP_LAUNCH_CHECK();
+    return MTP_OK;
+  }
   rownorm_kernel<<<(unsigned)M, 256, 0, s>>>(x, x_dt, gamma, g_dt, x_scale, (int)K, eps, mode, row_out, xo, xo_dt);
   MTP_LAUNCH_CHECK();
   return MTP_OK;

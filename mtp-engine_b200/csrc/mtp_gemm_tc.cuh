@@ -37,8 +37,8 @@ struct Cfg {
   static constexpr int A_BYTES = kBM * kKBlockBytes;
   static constexpr int B_BYTES = BN * kKBlockBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = (220 * 1024 / STAGE_BYTES) < 8 ? (220 * 1024 / STAGE_BYTES) : 8;
+  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;  // power of two >= 2*BN
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
 };
