@@ -138,9 +138,10 @@ int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   return MTP_OK;
 }
 
-// Tile width for a persistent launch: fewest (rounds x (BN + 16)) over the
-// instantiated widths, rounds = ceil(tiles / SMs); the +16 stands for the
-// fixed per-tile cost that favours wider tiles at equal rounds.
+// Tile width for a persistent launch.  The mainloop is bound by the shared-
+// memory operand traffic, which per K-block is (128 + BN) rows of 128 bytes,
+// so a launch costs about rounds x (128 + BN) with rounds = ceil(tiles/SMs);
+// the widest tile wins a tie.
 int pick_bn(int64_t M, int64_t N, int sms) {
   static const int cands[5] = {256, 224, 192, 160, 128};
   int best = 256;
@@ -149,7 +150,7 @@ int pick_bn(int64_t M, int64_t N, int sms) {
     if (bn > 128 && N <= 128) continue;
     const int64_t tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + bn - 1) / bn);
     const int64_t rounds = (tiles + sms - 1) / sms;
-    const int64_t cost = rounds * (bn + 16);
+    const int64_t cost = rounds * (bn + 128);
     if (cost < best_cost) {
       best_cost = cost;
       best = bn;
