@@ -304,13 +304,16 @@ def run_ours(args):
         return
 
     peaks = load_peaks()
+    # per-GPU rooflines: each rank does 1/world of every stage's work
+    w = float(world)
     kernels = {
-        "rmsnorm_linear": {"ms": s1, "bound": "tensor", "achieved": C2_FLOP / (s1 / 1e3) / 1e12,
-                           "unit": "TFLOP/s", "flop": C2_FLOP, "bytes": C2_BYTES},
-        "tree_attention_paged": {"ms": s2, "bound": "hbm", "achieved": C4_BYTES / (s2 / 1e3) / 1e9,
-                                 "unit": "GB/s", "bytes": C4_BYTES, "flop": C4_FLOP},
-        "fused_multi_verify": {"ms": s3, "bound": "tensor", "achieved": C5_FLOP / (s3 / 1e3) / 1e12,
-                               "unit": "TFLOP/s", "flop": C5_FLOP, "bytes": C5_BYTES},
+        "rmsnorm_linear": {"ms": s1, "bound": "tensor", "achieved": C2_FLOP / w / (s1 / 1e3) / 1e12,
+                           "unit": "TFLOP/s", "flop_per_gpu": C2_FLOP / w, "bytes_per_gpu": C2_BYTES / w},
+        "tree_attention_paged": {"ms": s2, "bound": "hbm", "achieved": C4_BYTES / w / (s2 / 1e3) / 1e9,
+                                 "unit": "GB/s", "bytes_per_gpu": C4_BYTES / w, "flop_per_gpu": C4_FLOP / w},
+        "fused_multi_verify": {"ms": s3, "bound": "tensor", "achieved": C5_FLOP / w / (s3 / 1e3) / 1e12,
+                               "unit": "TFLOP/s", "flop_per_gpu": C5_FLOP / w, "bytes_per_gpu": C5_BYTES / w,
+                               "note": "includes the NCCL key all-reduce when n_gpus > 1"},
     }
     for k in kernels.values():
         if k["bound"] == "hbm":
@@ -327,7 +330,8 @@ def run_ours(args):
         "peak": peaks["hbm"] if dom["bound"] == "hbm" else peaks["bf16_sus"],
         "unit": dom["unit"], "frac": dom["frac"],
         "peak_source": f"{peaks['src']} ({'hbm_gbs' if dom['bound'] == 'hbm' else 'bf16_tflops_sustained'})",
-        "traffic": profile_traffic(prof_name),
+        "traffic": profile_traffic(prof_name) if world == 1 else None,
+        "per": "GPU",
     }
     cpu = None
     if world == 1 and not args.no_cpu_baseline:

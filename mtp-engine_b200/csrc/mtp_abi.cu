@@ -143,11 +143,11 @@ int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
 // so a launch costs about rounds x (128 + BN) with rounds = ceil(tiles/SMs);
 // the widest tile wins a tie.
 int pick_bn(int64_t M, int64_t N, int sms) {
-  static const int cands[5] = {256, 224, 192, 160, 128};
+  static const int cands[6] = {256, 224, 192, 160, 128, 64};
   int best = 256;
   int64_t best_cost = INT64_MAX;
   for (int bn : cands) {
-    if (bn > 128 && N <= 128) continue;
+    if ((bn > 128 && N <= 128) || (bn > 64 && N <= 64)) continue;
     const int64_t tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + bn - 1) / bn);
     const int64_t rounds = (tiles + sms - 1) / sms;
     const int64_t cost = rounds * (bn + 128);
@@ -167,7 +167,8 @@ int launch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, in
     case 224: return launch_tc_inst<224, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
     case 192: return launch_tc_inst<192, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
     case 160: return launch_tc_inst<160, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
-    default: return launch_tc_inst<128, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    case 128: return launch_tc_inst<128, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    default: return launch_tc_inst<64, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
   }
 }
 
