@@ -270,11 +270,26 @@ def run_ours(args):
     h2d = sum(a.numel() * a.element_size() for a in (h_x, h_q, h_tk, h_tv, h_hid, h_dr))
     d2h = sum(a.numel() * a.element_size() for a in (o_acc, o_n, o_c))
 
+    # host->device copies run on a copy stream, each stage waiting only for
+    # its own inputs, so a later stage's upload overlaps an earlier stage
+    copy_stream = torch.cuda.Stream(dev)
+    groups = [((h_x, d_x),), ((h_q, d_q), (h_tk, d_tk), (h_tv, d_tv)), ((h_hid, d_hid), (h_dr, d_dr))]
+    step_start = torch.cuda.Event()
+    ready = [torch.cuda.Event() for _ in groups]
+
     def e2e_step():
-        for h, d_ in ((h_x, d_x), (h_q, d_q), (h_tk, d_tk), (h_tv, d_tv), (h_hid, d_hid), (h_dr, d_dr)):
-            d_.copy_(h, non_blocking=True)
+        step_start.record(stream)
+        copy_stream.wait_event(step_start)
+        with torch.cuda.stream(copy_stream):
+            for grp, ev_ in zip(groups, ready):
+                for h, d_ in grp:
+                    d_.copy_(h, non_blocking=True)
+                ev_.record(copy_stream)
+        stream.wait_event(ready[0])
         stage1(d_x)
+        stream.wait_event(ready[1])
         stage2(d_q, d_tk, d_tv)
+        stream.wait_event(ready[2])
         a, n_, c = stage3(d_hid, d_dr)
         o_acc.copy_(a, non_blocking=True)
         o_n.copy_(n_, non_blocking=True)
