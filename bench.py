@@ -96,7 +96,7 @@ class ClockSampler:
         self.gpu_ids = gpu_ids
 
     def start(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "20"]
         if self.gpu_ids:
             cmd += ["-i", ",".join(str(i) for i in self.gpu_ids)]
         try:
@@ -234,7 +234,7 @@ def run_ours(args):
     sampler = ClockSampler([local] if world == 1 else None) if rank == 0 else None
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+        time.sleep(0.2)
     launches0 = N.lib().mtp_launch_count()
     barrier()
     t_start.record(stream)
@@ -474,7 +474,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
