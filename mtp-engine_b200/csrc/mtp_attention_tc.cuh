@@ -88,6 +88,31 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1) as one packed f32x2 FMA
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// (s0, s1) += (a0, a1) as one packed f32x2 add
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 ra, rs;\n\t"
+      "mov.b64 rs, {%0, %1};\n\tmov.b64 ra, {%2, %3};\n\t"
+      "add.rn.f32x2 rs, rs, ra;\n\tmov.b64 {%0, %1}, rs;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi, int dtype) {
   if (dtype == MTP_DTYPE_BF16) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
@@ -116,8 +141,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* buf_full = bars + 1;
   uint64_t* buf_empty = buf_full + kNumBuf;
   uint64_t* s_full = buf_empty + kNumBuf;  // [2]
-  uint64_t* p_full = s_full + 2;           // [2]
-  uint64_t* pv_done = p_full + 2;          // [2]
+  uint64_t* p_full = s_full + 2;           // [2 tiles][2 halves of 64 keys]
+  uint64_t* pv_done = p_full + 4;          // [2]
   uint64_t* ids_full = pv_done + 2;        // [kIdRing]
   uint64_t* ids_empty = ids_full + kIdRing;  // [kIdRing]
   uint64_t* drain = ids_empty + kIdRing;
@@ -139,7 +164,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
+      mbar_init(&p_full[2 * t], 4);  // one arrival per softmax warp
+      mbar_init(&p_full[2 * t + 1], 4);
       mbar_init(&pv_done[t], 1);
     }
     for (int i = 0; i < kIdRing; ++i) {
@@ -277,12 +303,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16(d, sw128_kmajor_desc(qa + off), sw128_kmajor_desc(ka + off), IDESC_S, k > 0);
         }
       };
-      auto issue_pv = [&](int t, int buf, bool acc) {
+      // O_t += P_t V for keys [64*half, 64*half + 64) of the chunk
+      auto issue_pv = [&](int t, int buf, int half, bool acc) {
         const uint32_t d = tmem_base + (uint32_t)(256 + t * 128);
         const uint32_t pa = tmem_base + (uint32_t)(t * 128);  // P (bf16 pairs) over S_t's first 64 columns
         const uint32_t va = smem_u32(sBuf + buf * kTileBytes);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)  // 16 keys per MMA: 8 TMEM columns of P, 16 rows of V
+        for (int k = 4 * half; k < 4 * half + 4; ++k)  // 16 keys per MMA: 8 TMEM columns of P, 16 rows of V
           umma_f16_ts(d, pa + k * 8, sw128_mnmajor_desc(va + k * 16 * 128, kHalfBytes), IDESC_PV,
                       (acc || k > 0) ? 1u : 0u);
       };
@@ -297,14 +324,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < n_iter && ok; ++i) {
         const int kitem = 2 * i, vitem = 2 * i + 1, knext = 2 * i + 2;
         for (int t = 0; t < p.n_tiles && ok; ++t) {
-          if (!(ok = mbar_wait(&p_full[t], i & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(&p_full[2 * t], i & 1, abort_flag))) break;
           tc_fence_after();
-          ATTN_TRACE_IF(true, 4, t, i);
           if (t == 0) {
             if (!(ok = wait_item(vitem))) break;
             tc_fence_after();
           }
-          issue_pv(t, vitem % kNumBuf, i > 0);
+          issue_pv(t, vitem % kNumBuf, 0, i > 0);  // first 64 keys while the softmax finishes the rest
+          if (!(ok = mbar_wait(&p_full[2 * t + 1], i & 1, abort_flag))) break;
+          tc_fence_after();
+          ATTN_TRACE_IF(true, 4, t, i);
+          issue_pv(t, vitem % kNumBuf, 1, true);
           umma_commit(&pv_done[t]);
           ATTN_TRACE_IF(true, 2, t, 32 + (i & 31));
           if (t == p.n_tiles - 1) umma_commit(&buf_empty[vitem % kNumBuf]);
@@ -384,11 +414,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float m8[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(s[k]);
+      for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(s[k]), __uint_as_float(s[k + 8]));
 #pragma unroll
-      for (int j = 8; j < 128; ++j) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(s[j]));
-      const float mx = p.scale_log2 * fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                            fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      for (int j = 16; j < 128; j += 16)  // 3-input max: 8 chains, two new scores per step
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(s[j + k]), __uint_as_float(s[j + 8 + k]));
+      const float mx = p.scale_log2 * fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+                                            fmaxf(m8[6], m8[7]));
       const float mul = p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       if (i > 0) {
@@ -421,23 +453,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      // P = 2^(s*scale - m) as bf16 pairs, packed in place (s[j] is free once
+      // s[2j], s[2j+1] are read), written over S_t's first 64 columns in two
+      // halves so the MMA warp starts the first half of PV early.
+      float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {  // packed in place: s[j] is free once s[2j], s[2j+1] are read
-        const float e0 = ex2(fmaf(__uint_as_float(s[2 * j]), mul, -m_use));
-        const float e1 = ex2(fmaf(__uint_as_float(s[2 * j + 1]), mul, -m_use));
-        ls[j & 3] += e0 + e1;
-        s[j] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int j = 32 * h; j < 32 * h + 32; ++j) {
+          float x0, x1;
+          ffma2(x0, x1, __uint_as_float(s[2 * j]), __uint_as_float(s[2 * j + 1]), mul, mul, -m_use, -m_use);
+          const float e0 = ex2(x0), e1 = ex2(x1);
+          add2(ls0, ls1, e0, e1);
+          s[j] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
+        }
+        tmem_st32(s_addr + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * h]));
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[2 * t + h]);
       }
-      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      // P replaces the first 64 columns of S_t: the A operand of O_t += P V
-      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-      tmem_wait_st();
+      l_run += ls0 + ls1;
       ATTN_TRACE(3, t, i);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     if (ok && __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (n_iter - 1) & 1, abort_flag))) {
       tc_fence_after();
