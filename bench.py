@@ -219,15 +219,34 @@ def run_ours(args):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
-    # ---- warm-up
-    for _ in range(args.warmup):
-        stage1(x)
-        stage2(q, tk, tv)
-        stage3(hidden, draft)
+    # ---- warm-up (eager) on the stream the step runs on
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            stage1(x)
+            stage2(q, tk, tv)
+            stage3(hidden, draft)
+    stream.synchronize()
     barrier()
 
+    # ---- each stage captured once as a CUDA graph (kernel launches and, on
+    # N > 1, the NCCL all-reduce of the verify keys); replays cost one launch
+    launches0 = N.lib().mtp_launch_count()
+    graphs = []
+    if not args.no_graph:
+        for fn in (lambda: stage1(x), lambda: stage2(q, tk, tv), lambda: stage3(hidden, draft)):
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph, stream=stream):
+                out = fn()
+            graphs.append((gph, out))
+        stream.synchronize()
+        barrier()
+        launches_per_step = N.lib().mtp_launch_count() - launches0
+        run = [gph.replay for gph, _ in graphs]
+    else:
+        run = [lambda: stage1(x), lambda: stage2(q, tk, tv), lambda: stage3(hidden, draft)]
+
     # ---- timed region (device time, CUDA events on the launching stream)
-    stream = torch.cuda.current_stream(dev)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
@@ -237,19 +256,22 @@ def run_ours(args):
         time.sleep(0.2)
     launches0 = N.lib().mtp_launch_count()
     barrier()
-    t_start.record(stream)
-    for i in range(args.steps):
-        e = ev[i]
-        e[0].record(stream)
-        stage1(x)
-        e[1].record(stream)
-        stage2(q, tk, tv)
-        e[2].record(stream)
-        stage3(hidden, draft)
-        e[3].record(stream)
-    t_end.record(stream)
+    with torch.cuda.stream(stream):
+        t_start.record(stream)
+        for i in range(args.steps):
+            e = ev[i]
+            e[0].record(stream)
+            run[0]()
+            e[1].record(stream)
+            run[1]()
+            e[2].record(stream)
+            run[2]()
+            e[3].record(stream)
+        t_end.record(stream)
     barrier()
     launches = N.lib().mtp_launch_count() - launches0
+    if graphs:
+        launches = launches_per_step * args.steps  # graph replays launch the captured kernels
     clocks = sampler.stop() if sampler else None
     total_ms = t_start.elapsed_time(t_end)
     stage_ms = [sum(e[j].elapsed_time(e[j + 1]) for e in ev) / args.steps for j in range(3)]
@@ -263,7 +285,7 @@ def run_ours(args):
     # ---- end to end through the public API, host buffers in and out
     pin = lambda tt: tt.cpu().pin_memory()
     h_x, h_q, h_tk, h_tv, h_hid, h_dr = (pin(a) for a in (x, q, tk, tv, hidden, draft))
-    d_x, d_q, d_tk, d_tv, d_hid, d_dr = (torch.empty_like(a) for a in (x, q, tk, tv, hidden, draft))
+    d_x, d_q, d_tk, d_tv, d_hid, d_dr = x, q, tk, tv, hidden, draft  # the captured graphs read these
     o_acc = torch.empty((B5, S5 - 1), dtype=torch.int8).pin_memory()
     o_n = torch.empty((B5,), dtype=torch.int32).pin_memory()
     o_c = torch.empty((B5,), dtype=torch.int32).pin_memory()
@@ -285,15 +307,18 @@ def run_ours(args):
                 for h, d_ in grp:
                     d_.copy_(h, non_blocking=True)
                 ev_.record(copy_stream)
-        stream.wait_event(ready[0])
-        stage1(d_x)
-        stream.wait_event(ready[1])
-        stage2(d_q, d_tk, d_tv)
-        stream.wait_event(ready[2])
-        a, n_, c = stage3(d_hid, d_dr)
-        o_acc.copy_(a, non_blocking=True)
-        o_n.copy_(n_, non_blocking=True)
-        o_c.copy_(c, non_blocking=True)
+        with torch.cuda.stream(stream):
+            stream.wait_event(ready[0])
+            run[0]()
+            stream.wait_event(ready[1])
+            run[1]()
+            stream.wait_event(ready[2])
+            res = graphs[2][1] if graphs else None
+            out3 = run[2]()
+            a, n_, c = res if graphs else out3
+            o_acc.copy_(a, non_blocking=True)
+            o_n.copy_(n_, non_blocking=True)
+            o_c.copy_(c, non_blocking=True)
         stream.synchronize()
 
     for _ in range(max(1, args.warmup)):
@@ -305,6 +330,7 @@ def run_ours(args):
     for _ in range(args.steps):
         e2e_step()
     e1.record(stream)
+    stream.synchronize()
     barrier()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -312,6 +338,8 @@ def run_ours(args):
     e2e_value = TOKENS_PER_STEP * args.steps / (te.item() / 1e3)
 
     status = N.device_status(dev)
+    graphs.clear()  # graphs that hold NCCL calls go before the process group
+    torch.cuda.synchronize(dev)
     if rank != 0:
         if world > 1:
             dist.barrier(device_ids=[local])
@@ -478,6 +506,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch every call eagerly instead of graph replays")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
