@@ -231,18 +231,23 @@ def run_ours(args):
 
     # ---- each stage captured once as a CUDA graph (kernel launches and, on
     # N > 1, the NCCL all-reduce of the verify keys); replays cost one launch
+    # Graph replays are used on one GPU.  With N > 1 the stages launch
+    # eagerly unless --graph is given: a graph holding an NCCL call must be
+    # released before destroy_process_group (see the teardown below), and on
+    # 2-8 GPUs the replays saved only a few percent.
+    use_graphs = (world == 1 or args.graph) and not args.no_graph
     launches0 = N.lib().mtp_launch_count()
-    graphs = []
-    if not args.no_graph:
+    graphs = []  # the only owner of the graph objects
+    if use_graphs:
         for fn in (lambda: stage1(x), lambda: stage2(q, tk, tv), lambda: stage3(hidden, draft)):
-            gph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gph, stream=stream):
-                out = fn()
-            graphs.append((gph, out))
+            graphs.append(torch.cuda.CUDAGraph())
+            with torch.cuda.graph(graphs[-1], stream=stream):
+                outs = fn()
+            graphs[-1].outputs = outs
         stream.synchronize()
         barrier()
         launches_per_step = N.lib().mtp_launch_count() - launches0
-        run = [gph.replay for gph, _ in graphs]
+        run = [lambda i=i: graphs[i].replay() for i in range(3)]
     else:
         run = [lambda: stage1(x), lambda: stage2(q, tk, tv), lambda: stage3(hidden, draft)]
 
@@ -313,7 +318,7 @@ def run_ours(args):
             stream.wait_event(ready[1])
             run[1]()
             stream.wait_event(ready[2])
-            res = graphs[2][1] if graphs else None
+            res = graphs[2].outputs if graphs else None
             out3 = run[2]()
             a, n_, c = res if graphs else out3
             o_acc.copy_(a, non_blocking=True)
@@ -338,7 +343,12 @@ def run_ours(args):
     e2e_value = TOKENS_PER_STEP * args.steps / (te.item() / 1e3)
 
     status = N.device_status(dev)
-    graphs.clear()  # graphs that hold NCCL calls go before the process group
+    # graphs that hold NCCL calls must be gone before destroy_process_group:
+    # drop every reference (the list and the replay closures), then collect
+    run = None
+    graphs.clear()
+    import gc
+    gc.collect()
     torch.cuda.synchronize(dev)
     if rank != 0:
         if world > 1:
@@ -506,7 +516,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-graph", action="store_true", help="launch every call eagerly instead of graph replays")
+    ap.add_argument("--no-graph", action="store_true", help="launch every call eagerly")
+    ap.add_argument("--graph", action="store_true", help="also replay captured graphs when n_gpus > 1")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
