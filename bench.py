@@ -509,6 +509,137 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_sweep(args):
+    """--sweep: every BASELINE config timed on its own (one JSON line each,
+    marked "sweep"), 1 GPU.  L2 is flushed (256 MB write) between timed
+    calls; each call is bracketed by CUDA events on its stream; the median is
+    reported with its roofline fraction and a CPU-oracle baseline on a bounded
+    sample of the same config."""
+    import numpy as np
+    import torch
+
+    import _mtp_native as N
+    import mtp_fused_verify as mv
+    import mtp_kernels as mk
+    from oracle import mtp_oracle as O
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = load_peaks()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    f32 = lambda t: t.detach().float().cpu().numpy()
+
+    def time_call(fn, iters):
+        for _ in range(args.warmup):
+            fn()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+        return statistics.median(ts)
+
+    def cpu_time(fn, budget=8.0):
+        fn()
+        ts, t0 = [], time.perf_counter()
+        while not ts or (time.perf_counter() - t0 < budget and len(ts) < 5):
+            t1 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t1)
+        return statistics.median(ts)
+
+    def emit(name, units, unit, t, bound, achieved, peak, peak_src, cpu_units, cpu_t, extra=None):
+        line = {"sweep": True, "config": name, "metric": f"{unit} ({name})", "value": units / t, "unit": unit,
+                "ms": t * 1e3, "dtype": extra.pop("dtype") if extra and "dtype" in extra else "bf16",
+                "roofline": {"bound": bound, "achieved": achieved, "peak": peak,
+                             "unit": "TFLOP/s" if bound == "tensor" else "GB/s", "frac": achieved / peak,
+                             "peak_source": peak_src},
+                "cpu_baseline": {"value": cpu_units / cpu_t, "unit": unit, "cores": _blas_threads(),
+                                 "kind": "port", "sample": f"{cpu_units} units"}}
+        if extra:
+            line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    iters = max(5, min(args.steps, 50))
+    # ---- config 2 sweep: RMSNorm-linear bf16, gamma on
+    for M in (64, 512, 2048, 8192):
+        K, Nn = C2["K"], C2["N"]
+        g = torch.Generator(device=dev).manual_seed(1)
+        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        gam = 1.0 + 0.1 * torch.randn(K, generator=g, device=dev)
+        W = (0.02 * torch.randn(Nn, K, generator=g, device=dev)).to(torch.bfloat16)
+        t = time_call(lambda: mk.fused_rmsnorm_linear(x, W, None, C2["eps"], norm_weight=gam), iters)
+        flop, byts = 2.0 * M * Nn * K, 2.0 * (M * K + Nn * K + M * Nn)
+        tensor = flop / byts > 281  # ridge of the measured peaks
+        rows = min(M, 16)
+        xs, ws, gs = f32(x[:rows]), f32(W), f32(gam)
+        ct = cpu_time(lambda: O.rmsnorm_linear(xs, ws * gs[None, :], None, C2["eps"], 1.0))
+        emit(f"config2_M{M}", M, "rows/s", t, "tensor" if tensor else "hbm",
+             flop / t / 1e12 if tensor else byts / t / 1e9, peaks["bf16_sus"] if tensor else peaks["hbm"],
+             "measured bf16_tflops_sustained" if tensor else "measured hbm_gbs", rows, ct)
+        del x, W
+    # ---- config 3: FP8 E4M3, per-token activations, packed per-channel weight scales
+    M, K, Nn = 1024, 8192, 28672
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn(M, K, generator=g, device=dev)
+    x = x * (448.0 / x.abs().amax(dim=1, keepdim=True))
+    xq, sx = mk.quantize_fp8_rows(x)
+    wq, sw = mk.quantize_fp8_rows(0.02 * torch.randn(Nn, K, generator=g, device=dev))
+    flat, offs = mk.pack_scales([sw])
+    swv = mk.unpack_scale_tensor(flat, offs, 0, (Nn,))
+    t = time_call(lambda: mk.fused_rmsnorm_linear_fp8(xq, wq, swv, x_scale=sx, out_dtype=torch.bfloat16), iters)
+    flop = 2.0 * M * Nn * K
+    rows = 4
+    xd = O.e4m3_bits_to_f32(xq[:rows].view(torch.uint8).cpu().numpy()) * f32(sx)[:rows, None]
+    wd = O.e4m3_bits_to_f32(wq.view(torch.uint8).cpu().numpy())
+    sws = f32(sw)
+    ct = cpu_time(lambda: O.rmsnorm_linear_fp8(xd, wd, sws, None, 1e-6))
+    emit("config3_fp8", M, "rows/s", t, "tensor", flop / t / 1e12, 2 * peaks["bf16_sus"],
+         "2 x measured bf16_tflops_sustained (nominal fp8:bf16 ratio; fp8 not measured)", rows, ct,
+         {"dtype": "e4m3"})
+    del x, xq, wq
+    # ---- config 4: paged tree attention
+    B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
+    _, tm = O.draft_tree(C4["depth"], C4["branches"], "tree")
+    T = tm.shape[0]
+    g = torch.Generator(device=dev).manual_seed(3)
+    kp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
+    vp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
+    perm = torch.randperm(P, generator=torch.Generator().manual_seed(3))
+    per = ctx // ps
+    table = torch.stack([perm[b * per:(b + 1) * per].repeat_interleave(ps) for b in range(B)]).to(torch.int32)
+    tdev = table.to(dev)
+    q = torch.randn(B, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+    tk = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+    tv = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+    tmd = torch.tensor(tm, device=dev)
+    t = time_call(lambda: mk.fused_tree_attention_paged(q, kp, vp, tdev, tk, tv, tmd), iters)
+    pages0 = table[0].view(-1, ps)[:, 0].long()
+    kps, vps = f32(kp[pages0.to(dev)][:, 0:1]), f32(vp[pages0.to(dev)][:, 0:1])
+    tab0 = np.repeat(np.arange(pages0.numel(), dtype=np.int32), ps)[None, :]
+    q0, tk0, tv0 = f32(q[0:1]), f32(tk[0:1]), f32(tv[0:1])
+    ct = cpu_time(lambda: O.tree_attention_paged_fast(q0, kps, vps, tab0, ctx, ps, tk0, tv0, tm, 1 / math.sqrt(D)))
+    emit("config4_tree_attention", B * T, "tree-node queries/s", t, "hbm", C4_BYTES / t / 1e9, peaks["hbm"],
+         "measured hbm_gbs", T, ct, {"tflops": C4_FLOP / t / 1e12})
+    del kp, vp
+    # ---- config 5: fused_multi_verify, tp = 1
+    Bv, S, K, V = C5["B"], C5["S"], C5["K"], C5["V"]
+    g = torch.Generator(device=dev).manual_seed(4)
+    hid = torch.randn(Bv, S, K, generator=g, device=dev).to(torch.bfloat16)
+    lm = (0.02 * torch.randn(V, K, generator=g, device=dev)).to(torch.bfloat16)
+    dr = torch.randint(0, V, (Bv, S - 1), device=dev, dtype=torch.int32)
+    t = time_call(lambda: mv.fused_multi_verify(hid, lm, dr), iters)
+    hs, lms, ds = f32(hid[:2]), f32(lm), dr[:2].cpu().numpy()
+    ct = cpu_time(lambda: O.fused_multi_verify(hs, lms, None, ds))
+    emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16_sus"],
+         "measured bf16_tflops_sustained", 2 * S, ct)
+    assert N.device_status(dev) == 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -519,11 +650,14 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch every call eagerly")
     ap.add_argument("--graph", action="store_true", help="also replay captured graphs when n_gpus > 1")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--sweep", action="store_true", help="time every BASELINE config on its own (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.sweep:
+        run_sweep(args)
     else:
         run_ours(args)
 
