@@ -9,10 +9,12 @@
 #include <atomic>
 #include <mutex>
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 
 #include "mtp_attention.cuh"
 #include "mtp_attention_tc.cuh"
+#include "mtp_attention_tc2.cuh"
 #include "mtp_gemm_simt.cuh"
 #include "mtp_gemm_tc.cuh"
 #include "mtp_rownorm.cuh"
@@ -488,21 +490,25 @@ struct TreePlan {
   size_t ws_bytes = 256;
 };
 
+// chunk: keys per chunk of the kernel the plan is for (128 for
+// tree_attention_tc_kernel, 64 for tree_attention_tc2_kernel).
 TreePlan tree_plan(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t ctx_len, int64_t page_size,
-                   int64_t num_pages, int dtype) {
+                   int64_t num_pages, int dtype, int chunk = attn::kChunk) {
   TreePlan pl;
   if (!(dtype == MTP_DTYPE_BF16 || dtype == MTP_DTYPE_F16) || D != attn::kD || Hkv <= 0 || Hq % Hkv) return pl;
   const int64_t G = Hq / Hkv;
-  if (G <= 0 || attn::kChunk % G != 0 || T < 1 || T * G > 256) return pl;
-  if (!(page_size == 8 || page_size == 16 || page_size == 32 || page_size == 64 || page_size == 128)) return pl;
+  if (G <= 0 || 128 % G != 0 || T < 1 || T * G > 256) return pl;  // two 128-row query tiles at most
+  if (!(page_size == 8 || page_size == 16 || page_size == 32 || page_size == 64 || page_size == 128) ||
+      page_size > chunk)
+    return pl;
   if (num_pages * B * Hkv * page_size >= (int64_t)INT32_MAX || B * Hkv >= INT32_MAX / 4 || T > 4096 ||
       ctx_len >= (int64_t)INT32_MAX / 2)
     return pl;
   pl.G = (int)G;
   pl.t_per_tile = (int)(128 / G);
   pl.n_tiles = (int)((T * G + 127) / 128);
-  pl.n_ctx_chunks = (int)((ctx_len + attn::kChunk - 1) / attn::kChunk);
-  pl.n_chunks = pl.n_ctx_chunks + (int)((T + attn::kChunk - 1) / attn::kChunk);
+  pl.n_ctx_chunks = (int)((ctx_len + chunk - 1) / chunk);
+  pl.n_chunks = pl.n_ctx_chunks + (int)((T + chunk - 1) / chunk);
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = sm_count(dev >= 0 && dev < kMaxDevices ? dev : 0);
@@ -543,11 +549,31 @@ int make_map(CUtensorMap* map, const void* base, int dtype, int rank, const uint
   return MTP_OK;
 }
 
+// MTP_ATTN_KERNEL=2 selects tree_attention_tc2_kernel (64-key chunks,
+// double-buffered scores); anything else the 128-key kernel.
+int attn_kernel_version() {
+  static const int v = [] {
+    const char* e = getenv("MTP_ATTN_KERNEL");
+    return (e && e[0] == '2' && e[1] == 0) ? 2 : 1;
+  }();
+  return v;
+}
+
+template <typename Kern>
+int set_smem_once(Kern kern, int bytes, bool* done, int dev) {
+  if (!done[dev]) {
+    MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev] = true;
+  }
+  return MTP_OK;
+}
+
 int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pages, const void* v_pages,
                              const int32_t* page_table, int64_t table_stride, int64_t ctx_len, const void* tree_k,
                              const void* tree_v, const float* tree_mask, void* out, int dtype, int64_t B, int64_t T,
                              int64_t Hq, int64_t Hkv, int64_t num_pages, int64_t page_size, float scale,
-                             void* workspace, cudaStream_t s) {
+                             void* workspace, cudaStream_t s, int version) {
+  const int chunk = version == 2 ? attn2::kChunk : attn::kChunk;
   const uint64_t D = attn::kD, E = 2;
   CUtensorMap tq, tk, tv, ttk, ttv;
   {
@@ -570,7 +596,7 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
   {
     const uint64_t dims[3] = {D, (uint64_t)T, (uint64_t)(B * Hkv)};
     const uint64_t str[2] = {D * E, (uint64_t)T * D * E};
-    const uint32_t box[3] = {64, (uint32_t)attn::kChunk, 1};
+    const uint32_t box[3] = {64, (uint32_t)chunk, 1};
     if (int st = make_map(&ttk, tree_k, dtype, 3, dims, str, box)) return st;
     if (int st = make_map(&ttv, tree_v, dtype, 3, dims, str, box)) return st;
   }
@@ -604,21 +630,20 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
   int dev;
   if (int st = current_device(&dev)) return st;
   const int grid = (int)(B * Hkv * pl.splits);
-  if (dtype == MTP_DTYPE_BF16) {
-    static bool attr[kMaxDevices] = {false};
-    if (!attr[dev]) {
-      MTP_CUDA_TRY(cudaFuncSetAttribute(attn::tree_attention_tc_kernel<1>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes));
-      attr[dev] = true;
+  static bool attr[4][kMaxDevices] = {};
+  if (version == 2) {
+    if (dtype == MTP_DTYPE_BF16) {
+      if (int st = set_smem_once(attn2::tree_attention_tc2_kernel<1>, attn2::kSmemBytes, attr[2], dev)) return st;
+      attn2::tree_attention_tc2_kernel<1><<<grid, attn2::kThreads, attn2::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
+    } else {
+      if (int st = set_smem_once(attn2::tree_attention_tc2_kernel<0>, attn2::kSmemBytes, attr[3], dev)) return st;
+      attn2::tree_attention_tc2_kernel<0><<<grid, attn2::kThreads, attn2::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
     }
+  } else if (dtype == MTP_DTYPE_BF16) {
+    if (int st = set_smem_once(attn::tree_attention_tc_kernel<1>, attn::kSmemBytes, attr[0], dev)) return st;
     attn::tree_attention_tc_kernel<1><<<grid, attn::kThreads, attn::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
   } else {
-    static bool attr[kMaxDevices] = {false};
-    if (!attr[dev]) {
-      MTP_CUDA_TRY(cudaFuncSetAttribute(attn::tree_attention_tc_kernel<0>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes));
-      attr[dev] = true;
-    }
+    if (int st = set_smem_once(attn::tree_attention_tc_kernel<0>, attn::kSmemBytes, attr[1], dev)) return st;
     attn::tree_attention_tc_kernel<0><<<grid, attn::kThreads, attn::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
   }
   MTP_LAUNCH_CHECK();
@@ -636,9 +661,11 @@ extern "C" {
 
 size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
                                           int64_t ctx_len) {
-  // page_size 16 / bf16 give the same plan as every other eligible case of these sizes
-  const TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, 16, 1, MTP_DTYPE_BF16);
-  return pl.ws_bytes;
+  // page_size 16 / bf16 give the same plan as every other eligible case of
+  // these sizes; the larger of the two kernels' needs
+  const TreePlan p1 = tree_plan(B, T, Hq, Hkv, D, ctx_len, 16, 1, MTP_DTYPE_BF16, attn::kChunk);
+  const TreePlan p2 = tree_plan(B, T, Hq, Hkv, D, ctx_len, 16, 1, MTP_DTYPE_BF16, attn2::kChunk);
+  return p1.ws_bytes > p2.ws_bytes ? p1.ws_bytes : p2.ws_bytes;
 }
 
 int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_pages, const int32_t* page_table,
@@ -654,7 +681,13 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
   if (B * T == 0) return MTP_OK;
   if (!q || !out || !tree_k || !tree_v || !tree_mask || (ctx_len > 0 && (!k_pages || !v_pages || !page_table)))
     return fail(MTP_ERR_ARG, "null tensor pointer");
-  const TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype);
+  int version = attn_kernel_version();
+  TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype,
+                          version == 2 ? attn2::kChunk : attn::kChunk);
+  if (version == 2 && !pl.eligible) {  // e.g. 128-token pages: the 128-key kernel takes them
+    version = 1;
+    pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype, attn::kChunk);
+  }
   const bool aligned = aligned16(q) && aligned16(out) && aligned16(tree_k) && aligned16(tree_v) &&
                        (ctx_len == 0 || (aligned16(k_pages) && aligned16(v_pages)));
   if (pl.eligible && aligned && scale > 0.f) {  // the kernel folds a positive scale into exp2
@@ -662,7 +695,7 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
       return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", pl.ws_bytes);
     return launch_tree_attention_tc(pl, q, k_pages, v_pages, page_table, table_stride, ctx_len, tree_k, tree_v,
                                     tree_mask, out, dtype, B, T, Hq, Hkv, num_pages, page_size, scale, workspace,
-                                    as_stream(stream));
+                                    as_stream(stream), version);
   }
   AttnArgs a{};
   a.kind = ATTN_TREE_PAGED;
