@@ -212,7 +212,7 @@ def run_ours(args):
     def stage3(hh, dd):
         if world == 1:
             return mv.fused_multi_verify(hh, lm, dd)
-        return mp.vocab_parallel_multi_verify(hh, lm, dd, None, lo, prim)
+        return mp.vocab_parallel_multi_verify(hh, lm, dd, None, lo, prim, exchange=args.exchange)
 
     def barrier():
         if world > 1:
@@ -347,6 +347,7 @@ def run_ours(args):
     # drop every reference (the list and the replay closures), then collect
     run = None
     graphs.clear()
+    mp._EXCHANGES.clear()  # symmetric-memory buffers go before the process group too
     import gc
     gc.collect()
     torch.cuda.synchronize(dev)
@@ -651,6 +652,8 @@ def main():
     ap.add_argument("--graph", action="store_true", help="also replay captured graphs when n_gpus > 1")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--sweep", action="store_true", help="time every BASELINE config on its own (1 GPU)")
+    ap.add_argument("--exchange", choices=["nccl", "p2p"], default="nccl",
+                    help="vocab-parallel key exchange on N > 1: NCCL all-reduce or the peer-memory kernel")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

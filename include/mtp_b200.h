@@ -212,6 +212,22 @@ int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* 
                                    int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S, int64_t K,
                                    int64_t V, void* stream);
 
+/* Vocab-parallel verify, steps 2+3 fused, over peer memory instead of a
+ * collective library (replaces the all-reduce that would gather
+ * RowParallelLinear's shards, mtp_parallel.py:114-118).  Each rank owns a
+ * buffer of mtp_verify_exchange_bytes(B*S, world) bytes mapped into every
+ * rank (symmetric memory, zero-filled once); peer_bufs is a device array of
+ * the world buffer addresses, indexed by rank.  One kernel pushes this rank's
+ * keys[B*S] (from mtp_verify_shard_keys) into every peer over NVLink,
+ * publishes a per-call flag, waits (bounded) for every rank's keys, takes
+ * the max and writes the outputs of mtp_fused_multi_verify; keys are reset
+ * to INT64_MIN.  epoch is a device uint64 that starts at 0 on every rank;
+ * all ranks must make the same sequence of calls. */
+size_t mtp_verify_exchange_bytes(int64_t rows, int world);
+int mtp_verify_exchange_chain(int64_t* keys, const void* peer_bufs, int rank, int world, uint64_t* epoch,
+                              const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected,
+                              int64_t B, int64_t S, void* stream);
+
 /* Fills keys[n] with INT64_MIN. */
 int mtp_keys_fill(int64_t* keys, int64_t n, void* stream);
 

@@ -52,6 +52,8 @@ SIGNATURES = {
     "mtp_verify_shard_keys": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp]),
     "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
+    "mtp_verify_exchange_bytes": (_sz, [_i64, _i]),
+    "mtp_verify_exchange_chain": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_launch_count": (ctypes.c_uint64, []),
     "mtp_gemm_test": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _i, _vp]),
     "mtp_fused_multi_verify_noalloc": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64,

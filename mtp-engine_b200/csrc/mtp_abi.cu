@@ -861,6 +861,35 @@ int mtp_verify_shard_keys(const void* hidden, int h_dtype, const void* weight_sh
   return launch_gemm(hidden, h_dtype, weight_shard, w_dtype, M, V_shard, K, ep, as_stream(stream));
 }
 
+size_t mtp_verify_exchange_bytes(int64_t rows, int world) {
+  if (rows < 0 || world < 1) return 0;
+  return (size_t)2 * world * rows * 8 + (size_t)2 * world * 8;
+}
+
+int mtp_verify_exchange_chain(int64_t* keys, const void* peer_bufs, int rank, int world, uint64_t* epoch,
+                              const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected,
+                              int64_t B, int64_t S, void* stream) {
+  if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1");
+  if (world < 1 || rank < 0 || rank >= world) return fail(MTP_ERR_ARG, "rank %d / world %d", rank, world);
+  if (B == 0) return MTP_OK;
+  if (!keys || !peer_bufs || !epoch || (S > 1 && (!draft || !accept)) || !accepted_n || !corrected)
+    return fail(MTP_ERR_ARG, "null pointer");
+  GemmEpilogue ep{};
+  ep.mode = EPI_ARGMAX;
+  ep.finalize = FIN_CHAIN;
+  ep.draft = draft;
+  ep.accept = accept;
+  ep.accepted_n = accepted_n;
+  ep.tokens = corrected;
+  ep.B = B;
+  ep.S = S;
+  verify_exchange_chain_kernel<<<1, 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<long long*>(keys), static_cast<const unsigned long long*>(peer_bufs), rank, world,
+      reinterpret_cast<unsigned long long*>(epoch), ep);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
 int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* accept, int32_t* accepted_n,
                                int32_t* corrected, int64_t B, int64_t S, void* stream) {
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1");

@@ -75,6 +75,92 @@ __global__ void verify_finalize_kernel(GemmEpilogue ep) {
   verify_finalize(ep, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
 
+// ---------------------------------------------------------------------------
+// Vocab-parallel key exchange over peer memory (the NCCL all-reduce's job, in
+// one kernel, followed by the acceptance scan).  Every rank owns a buffer of
+//   keys  [2 parities][world][rows] int64, then flags [2 parities][world] uint64
+// mapped into every peer (symmetric memory); peers[r] is rank r's buffer.
+// Call e (a per-rank device counter, identical on all ranks because every
+// rank makes the same calls) uses parity e & 1: this rank stores its local
+// keys into slot [rank] of every peer's buffer with plain stores over NVLink,
+// fences at system scope, releases flag [rank] = e in every peer, waits until
+// its own flags of all ranks reach e (bounded: 2 s, then MTP_ERR_TIMEOUT),
+// and decodes the max over ranks.  A rank can only reach call e+2 after every
+// rank has started call e+1, i.e. after every rank finished reading call e,
+// so two parities suffice.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256)
+    verify_exchange_chain_kernel(long long* local_keys, const unsigned long long* peers, int rank, int world,
+                                 unsigned long long* epoch_counter, GemmEpilogue ep) {
+  __shared__ unsigned long long s_epoch;
+  __shared__ int s_ok;
+  const int64_t rows = ep.B * ep.S;
+  if (threadIdx.x == 0) {
+    s_epoch = ++(*epoch_counter);
+    s_ok = 1;
+  }
+  __syncthreads();
+  const unsigned long long e = s_epoch;
+  const int par = (int)(e & 1ull);
+  auto keys_of = [&](unsigned long long base, int slot) {
+    return reinterpret_cast<long long*>(base) + ((int64_t)par * world + slot) * rows;
+  };
+  auto flags_of = [&](unsigned long long base) {
+    return reinterpret_cast<unsigned long long*>(reinterpret_cast<long long*>(base) + 2 * (int64_t)world * rows) +
+           (int64_t)par * world;
+  };
+  // 1. push this rank's keys into every peer (its own buffer included)
+  for (int p = 0; p < world; ++p) {
+    long long* dst = keys_of(peers[p], rank);
+    for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) dst[r] = local_keys[r];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int p = 0; p < world; ++p) st_release_sys_u64(flags_of(peers[p]) + rank, e);
+  // 2. wait for every rank's keys in this rank's buffer
+  if (threadIdx.x < world) {
+    const unsigned long long* f = flags_of(peers[rank]) + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys_u64(f) < e) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_error(MTP_ERR_TIMEOUT);
+        s_ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  // 3. max over ranks, then the acceptance scan into the outputs
+  long long* mine = keys_of(peers[rank], 0);
+  for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
+    long long k = mine[r];
+    for (int p = 1; p < world; ++p) {
+      const long long o = mine[(int64_t)p * rows + r];
+      k = o > k ? o : k;
+    }
+    local_keys[r] = k;  // reduced key; verify_finalize reads then resets it
+  }
+  __threadfence_block();
+  __syncthreads();
+  if (s_ok) {
+    GemmEpilogue f = ep;
+    f.keys = local_keys;
+    verify_finalize(f, threadIdx.x, blockDim.x);
+  } else {
+    for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) local_keys[r] = KEY_EMPTY;
+  }
+}
+
 __global__ void keys_fill_kernel(long long* keys, int64_t n, unsigned int* counter) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) keys[i] = KEY_EMPTY;

@@ -24,6 +24,7 @@ mtp_parallel.py:84-118) with an added ``verify`` method.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import List, Optional, Tuple
 
@@ -128,6 +129,41 @@ def _keys_buffer(dev: torch.device, rows: int) -> torch.Tensor:
     return buf[: rows * 8].view(torch.int64)
 
 
+class _PeerExchange:
+    """Symmetric-memory buffers for the peer-memory key exchange
+    (mtp_verify_exchange_chain): one buffer per rank, mapped into every rank,
+    plus this rank's device-side call counter.  Every rank must build it at the
+    same point and then make the same sequence of verify calls."""
+
+    def __init__(self, dev: torch.device, rows: int, prim: "ParallelPrimitives"):
+        import torch.distributed._symmetric_memory as symm
+
+        group = prim.group if prim.group is not None else torch.distributed.group.WORLD
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            symm.enable_symm_mem_for_group(group.group_name)
+        self.rows = rows
+        nbytes = _N.lib().mtp_verify_exchange_bytes(rows, prim.tp_size)
+        self.buf = symm.empty(-(-nbytes // 8), dtype=torch.int64, device=dev)
+        self.buf.zero_()
+        self.handle = symm.rendezvous(self.buf, group)
+        self.peers = int(self.handle.buffer_ptrs_dev)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
+        torch.cuda.synchronize(dev)
+        torch.distributed.barrier(group=group)  # every buffer zeroed before any rank writes
+
+
+_EXCHANGES = {}
+
+
+def _peer_exchange(dev: torch.device, rows: int, prim: "ParallelPrimitives") -> _PeerExchange:
+    key = (dev.index, id(prim.group), prim.tp_size)
+    ex = _EXCHANGES.get(key)
+    if ex is None or ex.rows < rows:
+        ex = _PeerExchange(dev, max(rows, ex.rows if ex else 0), prim)
+        _EXCHANGES[key] = ex
+    return ex
+
+
 def vocab_parallel_multi_verify(
     hidden: torch.Tensor,
     weight_shard: torch.Tensor,
@@ -135,6 +171,7 @@ def vocab_parallel_multi_verify(
     bias_shard: Optional[torch.Tensor] = None,
     vocab_offset: Optional[int] = None,
     prim: Optional[ParallelPrimitives] = None,
+    exchange: str = "nccl",
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """``fused_multi_verify`` with the lm_head split over the ranks of `prim`.
 
@@ -143,6 +180,12 @@ def vocab_parallel_multi_verify(
     `vocab_offset` (default: the torch.chunk offset of this rank, assuming
     equal shards).  Every rank returns the same (accept, accepted_n,
     corrected) as single-device ``fused_multi_verify`` on the full weight.
+
+    exchange: "nccl" -- all-reduce(MAX) of the keys through torch.distributed,
+    then the acceptance scan; "p2p" -- one kernel pushes the keys to every
+    peer over NVLink through symmetric memory, waits for the peers' keys and
+    runs the scan (no collective library call; every rank must use it for the
+    same sequence of calls).
     """
     prim = prim or get_parallel_primitives()
     hidden = hidden.contiguous()
@@ -169,11 +212,18 @@ def vocab_parallel_multi_verify(
             _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight_shard), _N.dtype_code(weight_shard),
             _N.ptr(bias_shard), _N.dtype_code(bias_shard) if bias_shard is not None else 0,
             _N.ptr(keys), rows, K, Vr, int(vocab_offset), stream), "mtp_verify_shard_keys")
-        if prim.tp_size > 1:
-            prim.all_reduce(keys, op=torch.distributed.ReduceOp.MAX)
-        _N.check(L.mtp_verify_chain_from_keys(
-            _N.ptr(keys), _N.ptr(draft), _N.ptr(accept), _N.ptr(accepted_n), _N.ptr(corrected), B, S, stream),
-            "mtp_verify_chain_from_keys")  # also puts the keys back to rest
+        if prim.tp_size > 1 and exchange == "p2p":
+            ex = _peer_exchange(dev, rows, prim)
+            _N.check(L.mtp_verify_exchange_chain(
+                _N.ptr(keys), ctypes.c_void_p(ex.peers), prim.rank, prim.tp_size, _N.ptr(ex.epoch),
+                _N.ptr(draft), _N.ptr(accept), _N.ptr(accepted_n), _N.ptr(corrected), B, S, stream),
+                "mtp_verify_exchange_chain")  # also puts the keys back to rest
+        else:
+            if prim.tp_size > 1:
+                prim.all_reduce(keys, op=torch.distributed.ReduceOp.MAX)
+            _N.check(L.mtp_verify_chain_from_keys(
+                _N.ptr(keys), _N.ptr(draft), _N.ptr(accept), _N.ptr(accepted_n), _N.ptr(corrected), B, S,
+                stream), "mtp_verify_chain_from_keys")  # also puts the keys back to rest
     except Exception:
         _N.drop_workspace(dev, _KEYS_WS)  # never reuse keys left mid-reduction
         raise
@@ -185,8 +235,10 @@ class VocabParallelVerify:
     returns the replicated (accept, accepted_n, corrected)."""
 
     def __init__(self, weight_shard: torch.Tensor, vocab_offset: Optional[int] = None,
-                 bias_shard: Optional[torch.Tensor] = None, prim: Optional[ParallelPrimitives] = None):
+                 bias_shard: Optional[torch.Tensor] = None, prim: Optional[ParallelPrimitives] = None,
+                 exchange: str = "nccl"):
         self.prim = prim or get_parallel_primitives()
+        self.exchange = exchange
         self.weight_shard = weight_shard.contiguous()
         self.bias_shard = None if bias_shard is None else bias_shard.contiguous()
         self.vocab_offset = self.prim.rank * self.weight_shard.shape[0] if vocab_offset is None else vocab_offset
@@ -202,7 +254,8 @@ class VocabParallelVerify:
     def __call__(self, hidden: torch.Tensor, draft: torch.Tensor,
                  bias_shard: Optional[torch.Tensor] = None):
         b = self.bias_shard if bias_shard is None else bias_shard
-        return vocab_parallel_multi_verify(hidden, self.weight_shard, draft, b, self.vocab_offset, self.prim)
+        return vocab_parallel_multi_verify(hidden, self.weight_shard, draft, b, self.vocab_offset, self.prim,
+                                           self.exchange)
 
 
 class RowParallelLinear(nn.Module):

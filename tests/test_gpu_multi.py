@@ -1,0 +1,88 @@
+"""Vocab-parallel verify on 2+ GPUs (NCCL ranks): both key exchanges --
+the NCCL all-reduce and the peer-memory kernel -- must return exactly what
+single-device fused_multi_verify returns on the full lm_head, on every rank,
+for several calls in a row.  Runs only with MTP_TEST_MULTI_GPU=1 and at least
+two visible GPUs (GPU only)."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ENABLED = os.environ.get("MTP_TEST_MULTI_GPU") == "1"
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, q):
+    import datetime
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    repo = os.path.dirname(here)
+    for p_ in (repo, os.path.join(repo, "mtp-engine_b200")):
+        if p_ not in sys.path:
+            sys.path.insert(0, p_)
+    import torch.distributed as dist
+    import mtp_fused_verify as mv
+    import mtp_parallel as mp
+    try:
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        prim = mp.ParallelPrimitives()
+        results = []
+        for call in range(3):
+            g = torch.Generator(device=dev).manual_seed(100 + call)  # same inputs on every rank
+            B, S, K, V = 8, 6, 512, 10007
+            hid = torch.randn(B, S, K, generator=g, device=dev).to(torch.bfloat16)
+            w = (0.05 * torch.randn(V, K, generator=g, device=dev)).to(torch.bfloat16)
+            draft = torch.randint(0, V, (B, S - 1), generator=g, device=dev, dtype=torch.int32)
+            ref = mv.fused_multi_verify(hid, w, draft)
+            shard, off = mp.shard_lm_head(w, world, rank)
+            for exchange in ("nccl", "p2p"):
+                got = mp.vocab_parallel_multi_verify(hid, shard, draft, None, off, prim, exchange=exchange)
+                torch.cuda.synchronize(dev)
+                same = all(torch.equal(a, b) for a, b in zip(got, ref))
+                results.append((call, exchange, same))
+        import _mtp_native as N
+        status = N.device_status(dev)
+        dist.barrier(device_ids=[rank])
+        mp._EXCHANGES.clear()
+        dist.destroy_process_group()
+        q.put((rank, results, status))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e), -1))
+
+
+@pytest.mark.skipif(not ENABLED or not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs MTP_TEST_MULTI_GPU=1 and two GPUs")
+def test_vocab_parallel_exchanges_match_single_device():
+    import torch.multiprocessing as tmp
+    world = 2
+    ctx = tmp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for rank, results, status in out:
+        assert isinstance(results, list), results
+        assert status == 0
+        for call, exchange, same in results:
+            assert same, f"rank {rank} call {call} exchange {exchange} differs from single-device verify"
