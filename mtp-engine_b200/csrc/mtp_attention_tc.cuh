@@ -32,7 +32,7 @@
 //               16 chunks ahead of the TMA producer (shared-memory ring).
 // Long contexts with few units are split over CTAs (flash-decoding); the
 // partial (O, max, sum) triples are merged by attn_merge_kernel.
-// Every wait is bounded (mbar_wait).  No clusters, no TMA multicast.
+// Every wait is bounded (mbar_wait).  No clusters; every TMA load fills its own CTA.
 #pragma once
 
 #include "mtp_common.cuh"

@@ -142,7 +142,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// ---- TMA (tensor-map bulk copies, no multicast) ---------------------------
+// ---- TMA (tensor-map bulk copies into this CTA only) ----------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
 }

@@ -20,7 +20,7 @@
 //               tile -- no logits ever reach HBM).
 // Tiles are numbered M-fastest so the CTAs that share a weight tile run at
 // the same time and the weight is read from HBM about once.
-// No TMA multicast and no clusters: the same kernel serves multi-GPU jobs.
+// No clusters; every TMA load fills its own CTA, so the same kernel serves multi-GPU jobs.
 #pragma once
 
 #include "mtp_verify.cuh"

@@ -140,12 +140,13 @@ __global__ void __launch_bounds__(256)
     }
   }
   __syncthreads();
-  // 3. max over ranks, then the acceptance scan into the outputs
-  long long* mine = keys_of(peers[rank], 0);
+  // 3. max over ranks, then the acceptance scan into the outputs.  Peers wrote
+  // these slots over NVLink into this GPU's L2: read them from L2 (__ldcg).
+  const long long* mine = keys_of(peers[rank], 0);
   for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
-    long long k = mine[r];
+    long long k = __ldcg(mine + r);
     for (int p = 1; p < world; ++p) {
-      const long long o = mine[(int64_t)p * rows + r];
+      const long long o = __ldcg(mine + (int64_t)p * rows + r);
       k = o > k ? o : k;
     }
     local_keys[r] = k;  // reduced key; verify_finalize reads then resets it
