@@ -41,7 +41,8 @@ constexpr int kItem = 2 * kHalf;                 // one K or V chunk, 16 KB
 constexpr int kNumBuf = 9;
 constexpr int kIdRing = 16;
 constexpr int kMaxPages = 8;                     // page_size >= 8
-constexpr int kSmemBytes = 2 * kQTile + kNumBuf * kItem + kIdRing * kMaxPages * 4 + 512 + 1024;
+constexpr int kBarBytes = 640;                   // 64 mbarriers + TMEM slot + abort flag
+constexpr int kSmemBytes = 2 * kQTile + kNumBuf * kItem + kIdRing * kMaxPages * 4 + kBarBytes + 1024;
 constexpr float kRescaleThreshold = 8.0f;
 
 template <int AB_FMT>
@@ -63,8 +64,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* buf_empty = buf_full + kNumBuf;    // [kNumBuf]
   uint64_t* s_full = buf_empty + kNumBuf;      // [tile][buffer]
   uint64_t* p_full = s_full + 4;               // [tile][buffer]
-  uint64_t* pv_done = p_full + 4;              // [tile]
-  uint64_t* ids_full = pv_done + 2;            // [kIdRing]
+  uint64_t* pv_done = p_full + 4;              // [tile], one phase per PV
+  uint64_t* o_done = pv_done + 2;              // [tile], completes once: after the last PV
+  uint64_t* ids_full = o_done + 2;             // [kIdRing]
   uint64_t* ids_empty = ids_full + kIdRing;    // [kIdRing]
   uint64_t* drain = ids_empty + kIdRing;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -87,8 +89,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);  // one arrival per softmax warp
     }
-    mbar_init(&pv_done[0], 1);
-    mbar_init(&pv_done[1], 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_done[t], 1);
+    }
     for (int i = 0; i < kIdRing; ++i) {
       mbar_init(&ids_full[i], 1);
       mbar_init(&ids_empty[i], 1);
@@ -245,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           issue_pv(t, sb, vitem % kNumBuf, i > 0);
           umma_commit(&pv_done[t]);
+          if (i == n_iter - 1) umma_commit(&o_done[t]);
           if (t == p.n_tiles - 1) umma_commit(&buf_empty[vitem % kNumBuf]);
           if (i + 2 < n_iter) {
             if (t == 0) {
@@ -368,7 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[2 * t + sb]);
     }
-    if (ok && __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (n_iter - 1) & 1, abort_flag))) {
+    // pv_done may be two phases behind here (the softmax waits on it only to
+    // rescale), so a parity wait on it could pass early: o_done completes once.
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done[t], 0, abort_flag))) {
       tc_fence_after();
       const int row_in_unit = t * 128 + r;
       if (p.splits == 1) {
