@@ -59,6 +59,57 @@ const char* mtp_last_error(void);
 int mtp_device_status(void* stream, int* code_out, int clear);
 
 /* ------------------------------------------------------------------------- */
+/* GEMM schedule (no counterpart in the reference, whose Triton kernels use  */
+/* one program per output tile)                                              */
+/* ------------------------------------------------------------------------- */
+
+/* Process-wide schedule of the tensor-core GEMM inside mtp_rmsnorm_linear,
+ * mtp_rmsnorm_linear_fp8, mtp_fused_verify and mtp_fused_multi_verify:
+ * 0 (default) = whole output tiles per CTA; 1 = stream-K, where the tiles
+ * of the last, part-empty round are cut along K between CTAs and their fp32
+ * partials summed in K order by the part that finishes last (deterministic,
+ * not bit-identical to schedule 0).  Schedule 1 applies only to calls whose
+ * workspace has room for it (mtp_gemm_streamk_bytes) and where it is
+ * estimated to be faster; other calls run schedule 0.  Returns MTP_ERR_ARG
+ * for other modes. */
+int mtp_set_gemm_schedule(int mode);
+int mtp_gemm_schedule(void);
+
+/* Extra workspace bytes that let a GEMM of C[M,N] = A[M,K] B[N,K]^T
+ * (ab_dtype: 16-bit or E4M3) run stream-K on the current device; 0 when it
+ * would not.  Add it to the operator's own workspace size.  The stream-K
+ * counters sit in the 16 KB that end 256 bytes before the end of the
+ * workspace and rest at INT64_MIN: fill a new workspace once with
+ * mtp_keys_fill over all of it (mtp_verify_workspace_init does this for
+ * verify workspaces); every call leaves them at rest.  After a call fails
+ * with MTP_ERR_TIMEOUT, fill the workspace again. */
+size_t mtp_gemm_streamk_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype);
+
+/* The counters and the final 256 bytes: a workspace that is reused for
+ * calls of other sizes under schedule 1 keeps at least this many bytes after
+ * the operator's own part, so no call writes over the counters. */
+#define MTP_STREAMK_TAIL_BYTES 16640
+
+/* Test support: the stream-K plan for `sms` SMs (grid > 0 forces the
+ * schedule on that many CTAs).  info[9] = {used, BN, grid, dp_rounds,
+ * dp_tiles, q (K blocks per CTA in the stream-K phase), tiles, K blocks per
+ * tile, workspace bytes}. */
+int mtp_gemm_streamk_plan(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms, int grid, int64_t* info);
+
+/* Test support, host only: walks the kernel's work iterator for every CTA of
+ * that plan and checks that each (tile, K block) is computed once and that
+ * split tiles' parts and slots agree.  MTP_OK or MTP_ERR_SHAPE (message in
+ * mtp_last_error). */
+int mtp_gemm_streamk_check(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms, int grid);
+
+/* Test support: C[M,N] (fp32) = A[M,K] @ B[N,K]^T through the stream-K
+ * kernel on `grid` CTAs (<= 0: one per SM), whatever the schedule setting.
+ * workspace: info[8] bytes of mtp_gemm_streamk_plan, filled once with
+ * INT64_MIN. */
+int mtp_gemm_test_streamk(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,
+                          int grid, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
 /* RMSNorm -> linear                                                          */
 /* ------------------------------------------------------------------------- */
 

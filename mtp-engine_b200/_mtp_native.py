@@ -54,6 +54,12 @@ SIGNATURES = {
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
     "mtp_verify_exchange_bytes": (_sz, [_i64, _i]),
     "mtp_verify_exchange_chain": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "mtp_set_gemm_schedule": (_i, [_i]),
+    "mtp_gemm_schedule": (_i, []),
+    "mtp_gemm_streamk_bytes": (_sz, [_i64, _i64, _i64, _i]),
+    "mtp_gemm_streamk_plan": (_i, [_i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_i64)]),
+    "mtp_gemm_streamk_check": (_i, [_i64, _i64, _i64, _i, _i, _i]),
+    "mtp_gemm_test_streamk": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _i, _vp, _sz, _vp]),
     "mtp_launch_count": (ctypes.c_uint64, []),
     "mtp_gemm_test": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _i, _vp]),
     "mtp_fused_multi_verify_noalloc": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
@@ -79,6 +85,8 @@ def lib() -> ctypes.CDLL:
                     fn = getattr(L, name)
                     fn.restype = res
                     fn.argtypes = args
+                if os.environ.get("MTP_GEMM_STREAMK") == "1":  # before any workspace exists
+                    L.mtp_set_gemm_schedule(1)
                 _lib = L
     return _lib
 
@@ -156,10 +164,60 @@ def drop_workspace(device: torch.device, name: str) -> None:
         _ws.pop(key, None)
 
 
-def verify_workspace(device: torch.device, rows: int) -> torch.Tensor:
-    """Keys + ticket counter for the fused verify kernels.  Initialised once;
-    every verify call leaves it initialised again."""
+# --------------------------------------------------------------------------- #
+# GEMM schedule (stream-K needs room in the workspace, see include/mtp_b200.h)
+# --------------------------------------------------------------------------- #
+STREAMK_TAIL = 16640  # MTP_STREAMK_TAIL_BYTES: counters + the final 256 bytes
+_GEMM_WS = ("rmsnorm_linear", "rmsnorm_linear_fp8")
+
+
+def _rest_fill(device: torch.device):
+    """Workspace init: every 8-byte word INT64_MIN (the stream-K counters'
+    resting value; the rest of an RMSNorm-linear workspace is overwritten by
+    every call)."""
+    def _init(buf):
+        check(lib().mtp_keys_fill(ptr(buf), buf.numel() // 8, stream_handle(device)), "mtp_keys_fill")
+    return _init
+
+
+def gemm_schedule() -> int:
+    return int(lib().mtp_gemm_schedule())
+
+
+def set_gemm_schedule(mode: int) -> None:
+    """0 = data-parallel tiles, 1 = stream-K where it is faster.  Cached
+    RMSNorm-linear workspaces are dropped: one used under schedule 0 may have
+    overwritten the counter tail."""
+    check(lib().mtp_set_gemm_schedule(int(mode)), "mtp_set_gemm_schedule")
+    with _ws_lock:
+        for key in [k for k in _ws if k[2] in _GEMM_WS]:
+            del _ws[key]
+
+
+def streamk_bytes(M: int, N: int, K: int, ab_code: int) -> int:
+    if gemm_schedule() != 1:
+        return 0
+    return int(lib().mtp_gemm_streamk_bytes(int(M), int(N), int(K), int(ab_code)))
+
+
+def gemm_workspace(device: torch.device, name: str, base: int, M: int, N: int, K: int,
+                   ab_code: int) -> torch.Tensor:
+    """Operator workspace of `base` bytes; under schedule 1 followed by the
+    stream-K slots and counters (at least the counter tail, so no call of
+    another size ever writes over the counters)."""
+    if gemm_schedule() != 1:
+        return workspace(device, name, base, _rest_fill(device))
+    extra = streamk_bytes(M, N, K, ab_code) or STREAMK_TAIL
+    return workspace(device, name, int(base) + extra, _rest_fill(device))
+
+
+def verify_workspace(device: torch.device, rows: int, N: int = 0, K: int = 0, ab_code: int = DT_BF16) -> torch.Tensor:
+    """Keys + ticket counter for the fused verify kernels (+ the stream-K
+    region for an [rows, K] x [N, K] GEMM under schedule 1).  Initialised
+    once; every verify call leaves it initialised again."""
     need = lib().mtp_verify_workspace(int(rows))
+    if N > 0 and K > 0:
+        need += streamk_bytes(rows, N, K, ab_code)
 
     def _init(buf):
         check(lib().mtp_verify_workspace_init(ptr(buf), buf.numel(), stream_handle(device)),

@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <vector>
 #include <stdarg.h>
 #include <stdlib.h>
 #include <stdio.h>
@@ -16,6 +17,7 @@
 #include "mtp_attention_tc.cuh"
 #include "mtp_attention_tc2.cuh"
 #include "mtp_gemm_simt.cuh"
+#include "mtp_gemm_sk.cuh"
 #include "mtp_gemm_tc.cuh"
 #include "mtp_rownorm.cuh"
 #include "mtp_verify.cuh"
@@ -174,9 +176,131 @@ int launch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, in
   }
 }
 
-// A [M,K] and B [N,K] both K-major, 16-bit (ab_dtype) or E4M3 (fp8).
+// ---------------------------------------------------------------- stream-K
+// Process-wide GEMM schedule: 0 = data-parallel tiles (default), 1 = the
+// stream-K schedule wherever its plan is cheaper and the caller's workspace
+// has room for it (mtp_set_gemm_schedule).
+std::atomic<int> g_gemm_schedule{0};
+
+// Stream-K counters: a fixed 16 KB ending 256 bytes before the end of the
+// workspace (the last 256 bytes are the verify ticket), so a workspace reused
+// for other sizes keeps them at rest; the partial slots need no init.
+constexpr size_t kSkCounterBytes = 16384;
+constexpr size_t kSkTail = kSkCounterBytes + 256;
+static_assert(kSkTail == MTP_STREAMK_TAIL_BYTES, "header and library disagree on the stream-K tail");
+
+struct SkPlan {
+  bool use = false;
+  int bn = 256;
+  int grid = 0;
+  sk::Sched s{};
+  size_t slot_bytes = 0;
+};
+
+// Cost in the units of pick_bn (K blocks x (128 + BN) rows of operand
+// traffic per CTA).  A part that arrives last reads each other part's slot
+// (128 x BN fp32 from L2, about 6 K blocks' worth at BN = 256), plus ~2 for
+// storing its own.  grid > 0 forces the schedule on that many CTAs (tests).
+SkPlan sk_plan(int64_t M, int64_t N, int num_kb, int sms, int grid) {
+  SkPlan p;
+  p.bn = N > 128 ? 256 : 128;
+  const int64_t num_m = (M + tc::kBM - 1) / tc::kBM, num_n = (N + p.bn - 1) / p.bn;
+  const int64_t T = num_m * num_n;
+  const int P = grid > 0 ? grid : sms;
+  if (T <= 0 || P <= 0 || num_kb <= 0 || T > INT32_MAX / 2) return p;
+  int64_t dp_rounds = T / P - 1;
+  if (dp_rounds < 0) dp_rounds = 0;
+  const int64_t sk_tiles = T - dp_rounds * P;
+  if (sk_tiles * 8 > (int64_t)kSkCounterBytes) return p;
+  const int64_t sk_total = sk_tiles * num_kb;
+  const int64_t q = (sk_total + P - 1) / P;
+  p.grid = P;
+  p.s.num_m = (int)num_m;
+  p.s.num_tiles = (int)T;
+  p.s.num_kb = num_kb;
+  p.s.dp_rounds = (int)dp_rounds;
+  p.s.dp_tiles = (int)(dp_rounds * P);
+  p.s.q = (int)q;
+  p.s.sk_total = sk_total;
+  p.slot_bytes = align256((size_t)2 * P * tc::kBM * p.bn * 4);
+  if (grid > 0) {
+    p.use = true;
+    return p;
+  }
+  if (T % P == 0) return p;  // whole rounds: nothing to balance
+  const int64_t max_parts = q >= num_kb ? 2 : (num_kb + q - 1) / q + 1;
+  const int64_t fix = (6 * (max_parts - 1) + 2) * p.bn / 256;
+  const int64_t cost_sk = (dp_rounds * num_kb + q + fix) * (p.bn + 128);
+  const int bn_dp = pick_bn(M, N, sms);
+  const int64_t t_dp = num_m * ((N + bn_dp - 1) / bn_dp);
+  const int64_t cost_dp = ((t_dp + sms - 1) / sms) * num_kb * (bn_dp + 128);
+  p.use = cost_sk * 100 < cost_dp * 97;
+  return p;
+}
+
+size_t sk_bytes_needed(const SkPlan& p) { return p.use ? p.slot_bytes + kSkTail : 0; }
+
+template <int BN, bool FP8, int FMT>
+int launch_sk_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, const SkPlan& pl,
+                   unsigned long long* counters, float* slots, const GemmEpilogue& ep, cudaStream_t s) {
+  auto kern = sk::gemm_sk_kernel<BN, FP8, FMT>;
+  // verify workspaces rest at INT64_MIN everywhere: clean the slots after use
+  const int clean_slots = ep.mode == EPI_ARGMAX ? 1 : 0;
+  constexpr int smem = tc::Cfg<BN>::SMEM_BYTES;
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  static bool attr_done[kMaxDevices] = {false};
+  if (!attr_done[dev]) {
+    MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done[dev] = true;
+  }
+  kern<<<pl.grid, tc::kThreads, smem, s>>>(ta, tb, M, N, pl.s, counters, slots, clean_slots, ep);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+// Stream-K launch when the schedule is on (or forced by sk_grid > 0) and the
+// region [sk_ws, sk_ws + sk_bytes) holds the slots followed by the counter
+// tail.  *launched stays false when the data-parallel kernel should run.
+int try_launch_sk(const void* A, const void* B, int ab_dtype, bool fp8, int64_t M, int64_t N, int64_t K,
+                  const GemmEpilogue& ep, cudaStream_t s, void* sk_ws, size_t sk_bytes, int sk_grid,
+                  bool* launched) {
+  *launched = false;
+  if (!sk_ws || (sk_grid <= 0 && g_gemm_schedule.load(std::memory_order_relaxed) != 1)) return MTP_OK;
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  const int eb = fp8 ? 1 : 2;
+  const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  const SkPlan pl = sk_plan(M, N, num_kb, sm_count(dev), sk_grid);
+  if (!pl.use || sk_bytes < sk_bytes_needed(pl)) return MTP_OK;
+  CUtensorMap ta, tb;
+  if (int st = make_kmajor_map(&ta, A, fp8, ab_dtype, M, K, tc::kBM)) return st;
+  if (int st = make_kmajor_map(&tb, B, fp8, ab_dtype, N, K, pl.bn)) return st;
+  uint8_t* base = static_cast<uint8_t*>(sk_ws);
+  float* slots = reinterpret_cast<float*>(base);
+  unsigned long long* counters = reinterpret_cast<unsigned long long*>(base + sk_bytes - kSkTail);
+  *launched = true;
+  const int m = (int)M, n = (int)N;
+  if (pl.bn == 256) {
+    if (fp8) return launch_sk_inst<256, true, 0>(ta, tb, m, n, pl, counters, slots, ep, s);
+    if (ab_dtype == MTP_DTYPE_BF16) return launch_sk_inst<256, false, 1>(ta, tb, m, n, pl, counters, slots, ep, s);
+    return launch_sk_inst<256, false, 0>(ta, tb, m, n, pl, counters, slots, ep, s);
+  }
+  if (fp8) return launch_sk_inst<128, true, 0>(ta, tb, m, n, pl, counters, slots, ep, s);
+  if (ab_dtype == MTP_DTYPE_BF16) return launch_sk_inst<128, false, 1>(ta, tb, m, n, pl, counters, slots, ep, s);
+  return launch_sk_inst<128, false, 0>(ta, tb, m, n, pl, counters, slots, ep, s);
+}
+
+// A [M,K] and B [N,K] both K-major, 16-bit (ab_dtype) or E4M3 (fp8).  With a
+// stream-K region (see try_launch_sk) the stream-K kernel may run instead.
 int launch_gemm_tc(const void* A, const void* B, int ab_dtype, bool fp8, int64_t M, int64_t N, int64_t K,
-                   const GemmEpilogue& ep, cudaStream_t s) {
+                   const GemmEpilogue& ep, cudaStream_t s, void* sk_ws = nullptr, size_t sk_bytes = 0,
+                   int sk_grid = 0) {
+  if (sk_ws || sk_grid > 0) {
+    bool launched = false;
+    if (int st = try_launch_sk(A, B, ab_dtype, fp8, M, N, K, ep, s, sk_ws, sk_bytes, sk_grid, &launched)) return st;
+    if (launched) return MTP_OK;
+  }
   int dev;
   if (int st = current_device(&dev)) return st;
   const int bn = pick_bn(M, N, sm_count(dev));
@@ -211,9 +335,9 @@ int launch_gemm_simt(const void* A, int a_dt, const void* B, int b_dt, int64_t M
 }
 
 int launch_gemm(const void* A, int a_dt, const void* B, int b_dt, int64_t M, int64_t N, int64_t K,
-                const GemmEpilogue& ep, cudaStream_t s) {
+                const GemmEpilogue& ep, cudaStream_t s, void* sk_ws = nullptr, size_t sk_bytes = 0) {
   if (tc_eligible(A, B, a_dt, b_dt, M, N, K))
-    return launch_gemm_tc(A, B, a_dt, a_dt == MTP_DTYPE_E4M3, M, N, K, ep, s);
+    return launch_gemm_tc(A, B, a_dt, a_dt == MTP_DTYPE_E4M3, M, N, K, ep, s, sk_ws, sk_bytes);
   return launch_gemm_simt(A, a_dt, B, b_dt, M, N, K, ep, s);
 }
 
@@ -321,6 +445,116 @@ int mtp_gemm_test(const void* A, const void* B, int ab_dtype, float* C, int64_t 
   return launch_gemm_simt(A, ab_dtype, B, ab_dtype, M, N, K, ep, as_stream(stream));
 }
 
+int mtp_set_gemm_schedule(int mode) {
+  if (mode != 0 && mode != 1) return fail(MTP_ERR_ARG, "GEMM schedule %d (expected 0 or 1)", mode);
+  g_gemm_schedule.store(mode, std::memory_order_relaxed);
+  return MTP_OK;
+}
+
+int mtp_gemm_schedule(void) { return g_gemm_schedule.load(std::memory_order_relaxed); }
+
+size_t mtp_gemm_streamk_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype) {
+  if (M <= 0 || N <= 0 || K <= 0 || !valid_dtype(ab_dtype) || ab_dtype == MTP_DTYPE_F32) return 0;
+  int dev;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  const int eb = ab_dtype == MTP_DTYPE_E4M3 ? 1 : 2;
+  const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  return sk_bytes_needed(sk_plan(M, N, num_kb, sm_count(dev), 0));
+}
+
+int mtp_gemm_streamk_plan(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms, int grid, int64_t* info) {
+  if (M <= 0 || N <= 0 || K <= 0 || sms <= 0 || !valid_dtype(ab_dtype) || !info)
+    return fail(MTP_ERR_ARG, "bad stream-K plan arguments");
+  const int eb = ab_dtype == MTP_DTYPE_E4M3 ? 1 : 2;
+  const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  const SkPlan p = sk_plan(M, N, num_kb, sms, grid);
+  const int64_t v[9] = {p.use ? 1 : 0, p.bn, p.grid, p.s.dp_rounds, p.s.dp_tiles, p.s.q, p.s.num_tiles,
+                        p.s.num_kb, (int64_t)(p.use || grid > 0 ? p.slot_bytes + kSkTail : 0)};
+  for (int i = 0; i < 9; ++i) info[i] = v[i];
+  return MTP_OK;
+}
+
+// Walks every CTA's work items on the host (the kernel's own iterator) and
+// checks that each (tile, K block) is computed exactly once, that every
+// split tile's parts are numbered 0..parts-1 in K order by consecutive CTAs,
+// and that the slot each part writes is the one the summing part reads.
+int mtp_gemm_streamk_check(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms, int grid) {
+  int64_t info[9];
+  if (int st = mtp_gemm_streamk_plan(M, N, K, ab_dtype, sms, grid, info)) return st;
+  const int eb = ab_dtype == MTP_DTYPE_E4M3 ? 1 : 2;
+  const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  const SkPlan p = sk_plan(M, N, num_kb, sms, grid);
+  if (p.grid <= 0) return fail(MTP_ERR_SHAPE, "no stream-K schedule for these sizes");
+  const sk::Sched& sc = p.s;
+  const int64_t T = sc.num_tiles;
+  if ((int64_t)(T - sc.dp_tiles) * 8 > (int64_t)kSkCounterBytes) return fail(MTP_ERR_SHAPE, "counter overflow");
+  std::vector<int> cover((size_t)T * num_kb, 0);
+  const int64_t cap = (int64_t)num_kb + 1;  // a tile has at most num_kb + 1 parts
+  std::vector<int> slot_of((size_t)((T - sc.dp_tiles) * cap), -1);  // [x][part]
+  std::vector<int> slot_used((size_t)2 * p.grid, 0);
+  std::vector<int> part_kb0((size_t)((T - sc.dp_tiles) * cap), -1);
+  for (int c = 0; c < p.grid; ++c) {
+    sk::Iter it;
+    it.init(sc, c, p.grid);
+    sk::Work w;
+    int splits = 0, items = 0;
+    while (it.next(sc, w)) {
+      if (++items > 1 << 20) return fail(MTP_ERR_SHAPE, "CTA %d: runaway iterator", c);
+      if (w.tile < 0 || w.tile >= T || w.kb0 < 0 || w.kb1 > num_kb || w.kb0 >= w.kb1)
+        return fail(MTP_ERR_SHAPE, "CTA %d: bad item tile %d kb [%d,%d)", c, w.tile, w.kb0, w.kb1);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) ++cover[(size_t)w.tile * num_kb + kb];
+      if (!w.split) continue;
+      ++splits;
+      if (w.x != w.tile - sc.dp_tiles || w.parts < 2 || w.parts > cap || w.part < 0 || w.part >= w.parts)
+        return fail(MTP_ERR_SHAPE, "CTA %d: bad split item x %d part %d/%d", c, w.x, w.part, w.parts);
+      if (w.slot < 0 || w.slot >= 2 * p.grid || slot_used[w.slot]++)
+        return fail(MTP_ERR_SHAPE, "CTA %d: slot %d reused", c, w.slot);
+      if (sk::part_slot(sc, w.x, w.part) != w.slot)
+        return fail(MTP_ERR_SHAPE, "tile %d part %d: written to slot %d, read from %d", w.tile, w.part, w.slot,
+                    sk::part_slot(sc, w.x, w.part));
+      const size_t at = (size_t)(w.x * cap + w.part);
+      if (slot_of[at] != -1) return fail(MTP_ERR_SHAPE, "tile %d part %d twice", w.tile, w.part);
+      slot_of[at] = w.slot;
+      part_kb0[at] = w.kb0;
+    }
+    if (splits > 2) return fail(MTP_ERR_SHAPE, "CTA %d has %d split items", c, splits);
+  }
+  for (int64_t i = 0; i < T * num_kb; ++i)
+    if (cover[i] != 1)
+      return fail(MTP_ERR_SHAPE, "tile %lld K block %lld computed %d times", (long long)(i / num_kb),
+                  (long long)(i % num_kb), cover[i]);
+  for (int64_t x = 0; x < T - sc.dp_tiles; ++x) {
+    const int parts = sk::tile_parts(sc, (int)x);
+    if (slot_of[(size_t)(x * cap)] == -1) continue;  // whole tile
+    for (int q = 0; q < parts; ++q) {
+      if (slot_of[(size_t)(x * cap + q)] == -1) return fail(MTP_ERR_SHAPE, "tile %lld part %d missing", (long long)x, q);
+      if (q > 0 && part_kb0[(size_t)(x * cap + q)] <= part_kb0[(size_t)(x * cap + q - 1)])
+        return fail(MTP_ERR_SHAPE, "tile %lld parts out of K order", (long long)x);
+    }
+  }
+  return MTP_OK;
+}
+
+int mtp_gemm_test_streamk(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,
+                          int grid, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int st = check_dims(M, N, K)) return st;
+  if (!valid_dtype(ab_dtype)) return fail(MTP_ERR_DTYPE, "bad dtype");
+  if (M == 0 || N == 0) return MTP_OK;
+  if (!A || !B || !C || !workspace) return fail(MTP_ERR_ARG, "null pointer");
+  if (!tc_eligible(A, B, ab_dtype, ab_dtype, M, N, K)) return fail(MTP_ERR_ALIGN, "operands not eligible");
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  const int g = grid > 0 ? (grid < sm_count(dev) ? grid : sm_count(dev)) : sm_count(dev);
+  const int eb = ab_dtype == MTP_DTYPE_E4M3 ? 1 : 2;
+  const SkPlan p = sk_plan(M, N, (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes), sm_count(dev), g);
+  if (p.grid <= 0) return fail(MTP_ERR_SHAPE, "no stream-K schedule for these sizes");
+  if (workspace_bytes < p.slot_bytes + kSkTail)
+    return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", p.slot_bytes + kSkTail);
+  GemmEpilogue ep = store_epilogue(nullptr, nullptr, nullptr, 0, 1.0f, C, MTP_DTYPE_F32, N);
+  return launch_gemm_tc(A, B, ab_dtype, ab_dtype == MTP_DTYPE_E4M3, M, N, K, ep, as_stream(stream), workspace,
+                        workspace_bytes, g);
+}
+
 int mtp_device_status(void* stream, int* code_out, int clear) {
   MTP_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
   int code = 0;
@@ -366,7 +600,9 @@ int mtp_rmsnorm_linear(const void* x, int x_dtype, const void* weight, int w_dty
   }
   GemmEpilogue ep = store_epilogue(rstd, nullptr, bias, bias_dtype, scale, y, y_dtype, N);
   const bool tc = x_dtype == w_dtype && x_dtype == y_dtype && tc_eligible(a, weight, x_dtype, w_dtype, M, N, K);
-  if (tc) return launch_gemm_tc(a, weight, x_dtype, false, M, N, K, ep, s);
+  if (tc)
+    return launch_gemm_tc(a, weight, x_dtype, false, M, N, K, ep, s, static_cast<uint8_t*>(workspace) + need,
+                          workspace_bytes - need);
   return launch_gemm_simt(a, x_dtype, weight, w_dtype, M, N, K, ep, s);
 }
 
@@ -411,7 +647,8 @@ int mtp_rmsnorm_linear_fp8(const void* x, int x_dtype, const float* x_scale, con
     a = xq;
   }
   GemmEpilogue ep = store_epilogue(rowf, wscale, bias, bias_dtype, 1.0f, y, y_dtype, N);
-  return launch_gemm(a, MTP_DTYPE_E4M3, weight, MTP_DTYPE_E4M3, M, N, K, ep, s);
+  return launch_gemm(a, MTP_DTYPE_E4M3, weight, MTP_DTYPE_E4M3, M, N, K, ep, s,
+                     static_cast<uint8_t*>(workspace) + need, workspace_bytes - need);
 }
 
 // ---------------------------------------------------------------- attention
@@ -761,7 +998,10 @@ static int verify_common(const void* hidden, int h_dtype, const void* weight, in
   ep.col_offset = 0;
   // the counter sits in the last 256 bytes of the workspace the caller sized
   ep.counter = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + workspace_bytes - 256);
-  return launch_gemm(hidden, h_dtype, weight, w_dtype, rows, V, K, ep, s);
+  // a larger workspace carries a stream-K region between the keys and the ticket
+  const size_t keys_bytes = align256((size_t)rows * 8);
+  return launch_gemm(hidden, h_dtype, weight, w_dtype, rows, V, K, ep, s, static_cast<uint8_t*>(workspace) + keys_bytes,
+                     workspace_bytes - keys_bytes);
 }
 
 int mtp_fused_verify(const void* hidden, int h_dtype, const void* weight, int w_dtype, const void* bias,

@@ -46,7 +46,7 @@ def fused_verify(
     top = torch.empty(M, dtype=torch.int32, device=hidden.device)
     if M == 0:
         return accept, top
-    ws = _N.verify_workspace(dev, M)
+    ws = _N.verify_workspace(dev, M, V, K, _N.dtype_code(hidden))
     _N.check(_N.lib().mtp_fused_verify(
         _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight), _N.dtype_code(weight),
         _N.ptr(bias), _N.dtype_code(bias) if bias is not None else 0,
@@ -80,7 +80,7 @@ def fused_multi_verify(
     corrected = torch.empty((B,), dtype=torch.int32, device=hidden.device)
     if B == 0:
         return accept, accepted_n, corrected
-    ws = _N.verify_workspace(dev, B * S)
+    ws = _N.verify_workspace(dev, B * S, V, K, _N.dtype_code(hidden))
     _N.check(_N.lib().mtp_fused_multi_verify(
         _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight), _N.dtype_code(weight),
         _N.ptr(bias), _N.dtype_code(bias) if bias is not None else 0,

@@ -102,7 +102,8 @@ def fused_rmsnorm_linear(
         assert norm_weight.shape == (K,), "norm_weight must have shape [K]"
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     L = _N.lib()
-    ws = _N.workspace(dev, "rmsnorm_linear", L.mtp_rmsnorm_linear_workspace(M, K, int(norm_weight is not None)))
+    ws = _N.gemm_workspace(dev, "rmsnorm_linear", L.mtp_rmsnorm_linear_workspace(M, K, int(norm_weight is not None)),
+                           M, N, K, _N.dtype_code(x))
     _N.check(L.mtp_rmsnorm_linear(
         _N.ptr(x), _N.dtype_code(x), _N.ptr(weight), _N.dtype_code(weight),
         _N.ptr(bias), _N.dtype_code(bias) if bias is not None else 0,
@@ -152,7 +153,8 @@ def fused_rmsnorm_linear_fp8(
         bias = bias.contiguous()
     y = torch.empty((M, N), dtype=out_dtype, device=x.device)
     L = _N.lib()
-    ws = _N.workspace(dev, "rmsnorm_linear_fp8", L.mtp_rmsnorm_linear_fp8_workspace(M, K))
+    ws = _N.gemm_workspace(dev, "rmsnorm_linear_fp8", L.mtp_rmsnorm_linear_fp8_workspace(M, K), M, N, K,
+                           _N.DT_E4M3)
     _N.check(L.mtp_rmsnorm_linear_fp8(
         _N.ptr(x), _N.dtype_code(x), _N.ptr(x_scale), _N.ptr(weight_fp8), _N.dtype_code(weight_fp8),
         _N.ptr(wscale), _N.ptr(bias), _N.dtype_code(bias) if bias is not None else 0,

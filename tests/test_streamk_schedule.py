@@ -1,0 +1,86 @@
+"""The stream-K GEMM schedule, checked on the host: the library walks the
+kernel's own work iterator (an __host__ __device__ function) for every CTA
+and verifies that each (tile, K block) is computed exactly once and that the
+slot every split part writes is the slot the summing part reads.  Also pins
+which benchmark shapes the cost model sends to stream-K.  No GPU needed."""
+
+import ctypes
+
+import pytest
+
+import _mtp_native as N
+
+SMS = 148  # B200
+
+
+def plan(M, Nn, K, dt=N.DT_BF16, sms=SMS, grid=0):
+    info = (ctypes.c_int64 * 9)()
+    N.check(N.lib().mtp_gemm_streamk_plan(M, Nn, K, dt, sms, grid, info), "mtp_gemm_streamk_plan")
+    keys = ("use", "bn", "grid", "dp_rounds", "dp_tiles", "q", "tiles", "num_kb", "bytes")
+    return dict(zip(keys, list(info)))
+
+
+def check(M, Nn, K, dt=N.DT_BF16, sms=SMS, grid=0):
+    st = N.lib().mtp_gemm_streamk_check(M, Nn, K, dt, sms, grid)
+    assert st == 0, N.lib().mtp_last_error().decode()
+
+
+# BASELINE workloads (one GPU, and one rank of 8) plus shapes that cut tiles
+# into many parts, leave CTAs without work, or have a single K block
+SHAPES = [
+    (384, 128256, 4096, N.DT_BF16),   # config 5 verify, 1 GPU
+    (384, 16032, 4096, N.DT_BF16),    # config 5 verify, 1 of 8 ranks
+    (512, 14336, 4096, N.DT_BF16),    # config 2 RMSNorm-linear, 1 GPU
+    (512, 1792, 4096, N.DT_BF16),     # config 2, 1 of 8 ranks
+    (1024, 14336, 4096, N.DT_E4M3),   # config 3 FP8
+    (64, 128256, 4096, N.DT_BF16),
+    (1, 300, 64, N.DT_BF16),
+    (129, 257, 4096, N.DT_F16),
+    (300, 1000, 1024, N.DT_E4M3),
+]
+
+
+@pytest.mark.parametrize("M,Nn,K,dt", SHAPES)
+@pytest.mark.parametrize("grid", [0, 1, 3, 7, 16, 148])
+def test_schedule_covers_every_block_once(M, Nn, K, dt, grid):
+    p = plan(M, Nn, K, dt, grid=grid)
+    if grid == 0 and not p["use"]:
+        pytest.skip("cost model keeps the data-parallel schedule")
+    check(M, Nn, K, dt, grid=grid)
+
+
+def test_cost_model_choices():
+    # verify, 1 GPU: 1503 tiles = 10.16 rounds -> 9 whole rounds + stream-K
+    p = plan(384, 128256, 4096)
+    assert p["use"] == 1 and p["bn"] == 256 and p["dp_rounds"] == 9 and p["tiles"] == 1503
+    assert p["q"] == -(-(1503 - 9 * 148) * 64 // 148)
+    # RMSNorm-linear, 1 GPU: 224 tiles = 1.51 rounds, all stream-K
+    p = plan(512, 14336, 4096)
+    assert p["use"] == 1 and p["dp_rounds"] == 0 and p["q"] == 97
+    # verify, 1 of 8 ranks: 189 tiles
+    assert plan(384, 16032, 4096)["use"] == 1
+    # RMSNorm-linear, 1 of 8 ranks: 28 tiles of 256 would be cut ~5 ways;
+    # the data-parallel schedule with narrower tiles is cheaper
+    assert plan(512, 1792, 4096)["use"] == 0
+    # whole rounds: nothing to balance
+    assert plan(128 * 148, 256, 4096)["use"] == 0
+
+
+def test_workspace_sizes():
+    p = plan(384, 128256, 4096)
+    assert p["bytes"] == 2 * 148 * 128 * 256 * 4 + N.STREAMK_TAIL
+    assert N.STREAMK_TAIL == 16640
+
+
+def test_schedule_switch_roundtrip():
+    L = N.lib()
+    assert L.mtp_gemm_schedule() in (0, 1)
+    before = L.mtp_gemm_schedule()
+    try:
+        N.set_gemm_schedule(1)
+        assert L.mtp_gemm_schedule() == 1
+        N.set_gemm_schedule(0)
+        assert L.mtp_gemm_schedule() == 0
+        assert L.mtp_set_gemm_schedule(2) == 8  # MTP_ERR_ARG
+    finally:
+        N.set_gemm_schedule(before)
