@@ -152,6 +152,7 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)  # before any workspace exists
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
@@ -399,7 +400,8 @@ def run_ours(args):
         "config": {"workload": WORKLOAD, "tokens_per_step": TOKENS_PER_STEP, "global_batch": C5["B"],
                    "seq_len": C5["S"],
                    "parallelism": "tp1" if world == 1 else f"tp{world} (cols / kv-heads / vocab)",
-                   "l2": "inputs larger than L2 (about 2.3 GB touched per step)"},
+                   "l2": "inputs larger than L2 (about 2.3 GB touched per step)",
+                   "gemm_schedule": args.gemm_schedule},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -526,6 +528,7 @@ def run_sweep(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
     peaks = load_peaks()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     f32 = lambda t: t.detach().float().cpu().numpy()
@@ -555,6 +558,7 @@ def run_sweep(args):
 
     def emit(name, units, unit, t, bound, achieved, peak, peak_src, cpu_units, cpu_t, extra=None):
         line = {"sweep": True, "config": name, "metric": f"{unit} ({name})", "value": units / t, "unit": unit,
+                "gemm_schedule": args.gemm_schedule,
                 "ms": t * 1e3, "dtype": extra.pop("dtype") if extra and "dtype" in extra else "bf16",
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak,
                              "unit": "TFLOP/s" if bound == "tensor" else "GB/s", "frac": achieved / peak,
@@ -654,6 +658,8 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="time every BASELINE config on its own (1 GPU)")
     ap.add_argument("--exchange", choices=["nccl", "p2p"], default="nccl",
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce or the peer-memory kernel")
+    ap.add_argument("--gemm-schedule", choices=["dp", "streamk"], default="dp",
+                    help="tensor-core GEMM schedule: whole tiles per CTA, or stream-K where it is faster")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
