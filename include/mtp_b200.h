@@ -234,6 +234,16 @@ int mtp_verify_shard_keys(const void* hidden, int h_dtype, const void* weight_sh
                           const void* bias_shard, int bias_dtype, int64_t* keys, int64_t M,
                           int64_t K, int64_t V_shard, int64_t vocab_offset, void* stream);
 
+/* mtp_verify_shard_keys with a stream-K region: under GEMM schedule 1 the
+ * shard's GEMM may run stream-K using [workspace, workspace +
+ * workspace_bytes), which holds mtp_gemm_streamk_bytes(M, V_shard, K,
+ * h_dtype) bytes filled once with INT64_MIN (every call leaves it so).
+ * workspace may be NULL (then identical to mtp_verify_shard_keys). */
+int mtp_verify_shard_keys_ws(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                             const void* bias_shard, int bias_dtype, int64_t* keys, int64_t M, int64_t K,
+                             int64_t V_shard, int64_t vocab_offset, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* Vocab-parallel verify, step 3: decode reduced keys [B*S] into the outputs
  * of mtp_fused_multi_verify and reset keys to INT64_MIN. */
 int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* accept,

@@ -50,6 +50,7 @@ SIGNATURES = {
     "mtp_fused_multi_verify": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                     _vp, _sz, _vp]),
     "mtp_verify_shard_keys": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "mtp_verify_shard_keys_ws": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
     "mtp_verify_exchange_bytes": (_sz, [_i64, _i]),

@@ -1101,6 +1101,27 @@ int mtp_verify_shard_keys(const void* hidden, int h_dtype, const void* weight_sh
   return launch_gemm(hidden, h_dtype, weight_shard, w_dtype, M, V_shard, K, ep, as_stream(stream));
 }
 
+int mtp_verify_shard_keys_ws(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                             const void* bias_shard, int bias_dtype, int64_t* keys, int64_t M, int64_t K,
+                             int64_t V_shard, int64_t vocab_offset, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  if (int st = check_dims(M, V_shard, K)) return st;
+  if (M == 0 || V_shard == 0) return MTP_OK;
+  if (vocab_offset < 0 || vocab_offset + V_shard > 0xFFFFFFFFLL) return fail(MTP_ERR_SHAPE, "vocab offset out of range");
+  if (!valid_dtype(h_dtype) || !valid_dtype(w_dtype) || h_dtype == MTP_DTYPE_E4M3 || w_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtype combination hidden=%d weight=%d", h_dtype, w_dtype);
+  if (!hidden || !weight_shard || !keys) return fail(MTP_ERR_ARG, "null tensor pointer");
+  GemmEpilogue ep{};
+  ep.mode = EPI_ARGMAX;
+  ep.bias = bias_shard;
+  ep.bias_dtype = bias_dtype;
+  ep.keys = reinterpret_cast<long long*>(keys);
+  ep.col_offset = vocab_offset;
+  ep.finalize = FIN_NONE;
+  return launch_gemm(hidden, h_dtype, weight_shard, w_dtype, M, V_shard, K, ep, as_stream(stream), workspace,
+                     workspace ? workspace_bytes : 0);
+}
+
 size_t mtp_verify_exchange_bytes(int64_t rows, int world) {
   if (rows < 0 || world < 1) return 0;
   return (size_t)2 * world * rows * 8 + (size_t)2 * world * 8;

@@ -119,14 +119,19 @@ def shard_lm_head(weight: torch.Tensor, world: int, rank: int) -> Tuple[torch.Te
 _KEYS_WS = "vocab_parallel_keys"
 
 
-def _keys_buffer(dev: torch.device, rows: int) -> torch.Tensor:
+def _keys_buffer(dev: torch.device, rows: int, sk_bytes: int = 0):
+    """This rank's keys [rows] int64, followed (under GEMM schedule 1) by the
+    stream-K region of the shard GEMM; the whole buffer rests at INT64_MIN.
+    Returns (keys, region, region_bytes)."""
     L = _N.lib()
 
     def _init(buf):
         _N.check(L.mtp_keys_fill(_N.ptr(buf), buf.numel() // 8, _N.stream_handle(dev)), "mtp_keys_fill")
 
-    buf = _N.workspace(dev, _KEYS_WS, rows * 8, _init)
-    return buf[: rows * 8].view(torch.int64)
+    keys_bytes = (rows * 8 + 255) // 256 * 256
+    buf = _N.workspace(dev, _KEYS_WS, keys_bytes + sk_bytes, _init)
+    region = buf[keys_bytes:] if sk_bytes > 0 else None
+    return buf[: rows * 8].view(torch.int64), region, (buf.numel() - keys_bytes) if sk_bytes > 0 else 0
 
 
 class _PeerExchange:
@@ -205,13 +210,15 @@ def vocab_parallel_multi_verify(
     accepted_n = torch.empty((B,), dtype=torch.int32, device=hidden.device)
     corrected = torch.empty((B,), dtype=torch.int32, device=hidden.device)
     L = _N.lib()
-    keys = _keys_buffer(dev, rows)  # at rest: every key is INT64_MIN
+    sk = _N.streamk_bytes(rows, Vr, K, _N.dtype_code(hidden))
+    keys, region, region_bytes = _keys_buffer(dev, rows, sk)  # at rest: every word is INT64_MIN
     stream = _N.stream_handle(dev)
     try:
-        _N.check(L.mtp_verify_shard_keys(
+        _N.check(L.mtp_verify_shard_keys_ws(
             _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight_shard), _N.dtype_code(weight_shard),
             _N.ptr(bias_shard), _N.dtype_code(bias_shard) if bias_shard is not None else 0,
-            _N.ptr(keys), rows, K, Vr, int(vocab_offset), stream), "mtp_verify_shard_keys")
+            _N.ptr(keys), rows, K, Vr, int(vocab_offset), _N.ptr(region), region_bytes, stream),
+            "mtp_verify_shard_keys_ws")
         if prim.tp_size > 1 and exchange == "p2p":
             ex = _peer_exchange(dev, rows, prim)
             _N.check(L.mtp_verify_exchange_chain(
