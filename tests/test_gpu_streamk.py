@@ -157,3 +157,32 @@ def test_fp8_schedules_agree(N):
     # E4M3 activations are not integers: only the fp32 summation order differs
     assert torch.allclose(got, ref, rtol=2e-2, atol=1e-3)
     assert N.device_status(d) == 0
+
+
+def test_shard_keys_streamk_matches(N):
+    import mtp_parallel as mp
+    B, S, K, V = 64, 6, 4096, 16032  # one rank of an 8-way config-5 verify: 189 tiles
+    hid, w, _ = _verify_inputs(B, S, K, V, seed=13)
+    rows = B * S
+    L = N.lib()
+    st = N.stream_handle(hid.device)
+    ref = torch.full((rows,), INT64_MIN, dtype=torch.int64, device=hid.device)
+    N.check(L.mtp_verify_shard_keys(N.ptr(hid), N.DT_BF16, N.ptr(w), N.DT_BF16, None, 0, N.ptr(ref), rows, K, V,
+                                    1000, st), "mtp_verify_shard_keys")
+    before = N.gemm_schedule()
+    try:
+        N.set_gemm_schedule(1)
+        sk = N.streamk_bytes(rows, V, K, N.DT_BF16)
+        assert sk > 0
+        for _ in range(2):
+            keys, region, region_bytes = mp._keys_buffer(hid.device, rows, sk)
+            N.check(L.mtp_verify_shard_keys_ws(N.ptr(hid), N.DT_BF16, N.ptr(w), N.DT_BF16, None, 0, N.ptr(keys),
+                                               rows, K, V, 1000, N.ptr(region), region_bytes, st),
+                    "mtp_verify_shard_keys_ws")
+            torch.cuda.synchronize()
+            assert torch.equal(keys, ref)
+            keys.fill_(INT64_MIN)  # what the decode step does
+            assert bool((region[: region_bytes - 256].view(torch.int64) == INT64_MIN).all())
+    finally:
+        N.set_gemm_schedule(before)
+    assert N.device_status(hid.device) == 0
