@@ -96,7 +96,6 @@ def test_multi_verify_schedules_agree_and_workspace_rests(N):
     import mtp_fused_verify as mv
     B, S, K, V = 64, 6, 4096, 128256  # config 5 sizes: 1503 tiles, stream-K on 148 SMs
     hid, w, draft = _verify_inputs(B, S, K, V, seed=11)
-    # drafts that hit: take the schedule-0 tops for half the rows
     before = N.gemm_schedule()
     try:
         N.set_gemm_schedule(0)
