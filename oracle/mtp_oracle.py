@@ -224,6 +224,36 @@ def tree_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray
     return np.einsum("bhl,bhld->bhd", p, vf).astype(np.float32)
 
 
+def tree_attn_rmsnorm_linear(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray,
+                             rms_w: Optional[np.ndarray], proj_w: np.ndarray,
+                             proj_bias: Optional[np.ndarray], wscale: Optional[np.ndarray],
+                             scale: float, eps: float) -> np.ndarray:
+    """``_eager_tree_attn_rmsnorm_linear``, mtp_kernels.py:881-905, which the
+    public ``fused_tree_attn_rmsnorm_linear`` (mtp_kernels.py:1222-1250)
+    calls unconditionally.
+
+    q [B,H,D], k/v [B,H,L,D], mask [L] (shared by every b, h); the attention
+    output stays float32 (no rounding to q.dtype, 884-895), then
+    ``attn * rsqrt(mean(attn**2) + eps) * rms_w`` (896-899; rms_w None = ones),
+    then ``attn @ (proj_w * wscale[:, None])^T + proj_bias`` (900-904).
+    A row whose keys are all masked is NaN, as in the reference.  Float32
+    result [B,H,N].
+    """
+    attn = tree_attention(q, k, v, mask, scale)  # the same softmax(q k^T) v, float32
+    D = attn.shape[-1]
+    rw = np.ones(D, np.float32) if rms_w is None else np.asarray(rms_w, dtype=np.float32)
+    with np.errstate(invalid="ignore"):
+        ms = (attn * attn).mean(axis=-1, keepdims=True)
+        attn = attn * (np.float32(1.0) / np.sqrt(ms + np.float32(eps))) * rw
+    w = np.asarray(proj_w, dtype=np.float32)
+    if wscale is not None:
+        w = w * np.asarray(wscale, dtype=np.float32)[:, None]
+    out = np.einsum("bhd,nd->bhn", attn, w)
+    if proj_bias is not None:
+        out = out + np.asarray(proj_bias, dtype=np.float32)
+    return out.astype(np.float32)
+
+
 def gather_paged_kv(pages: np.ndarray, page_table: np.ndarray, page_size: int,
                     L: Optional[int] = None) -> np.ndarray:
     """Per-token page gather of ``_eager_paged_attention``, mtp_kernels.py:839-848.

@@ -57,6 +57,7 @@ def save(name, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("MTP_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default="", help="write only this fixture (e.g. tree_attn_rmsnorm_linear)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     os.environ.setdefault("TRITON_INTERPRET", "1")
@@ -64,6 +65,10 @@ def main():
     import mtp_kernels as mk
     import mtp_fused_verify as mv
     from mtp_engine import SpeculativeDraftTree
+
+    if args.only == "tree_attn_rmsnorm_linear":
+        make_tree_attn_rmsnorm_linear(torch, mk)
+        return
 
     # ---------------------------------------------------------------- rmsnorm_linear fp32
     torch.manual_seed(1)  # test_engine.py:5
@@ -265,6 +270,40 @@ def main():
         arrs[key + "_parent"] = t.parent.numpy()
         arrs[key + "_mask"] = t.tree_mask.numpy()
     save("draft_tree.npz", **arrs)
+
+    make_tree_attn_rmsnorm_linear(torch, mk)
+
+
+def make_tree_attn_rmsnorm_linear(torch, mk):
+    """``_eager_tree_attn_rmsnorm_linear`` (mtp_kernels.py:881-905), the body
+    of ``fused_tree_attn_rmsnorm_linear`` (1222-1250).  Shapes: the
+    reference's memory bench geometry (bench_memory.py:96, H=4 D=64 L=32
+    N=256) with a partial mask, rms_w, bias and wscale; a bare case (no
+    rms_w / bias / wscale); a bf16 case; and an all-masked case (NaN rows)."""
+    torch.manual_seed(21)
+    B, H, D, L, N = 3, 4, 64, 32, 256
+    q = torch.randn(B, H, D)
+    k = torch.randn(B, H, L, D)
+    v = torch.randn(B, H, L, D)
+    mask = (torch.rand(L) > 0.4).float()
+    mask[0] = 1.0
+    rms_w = 1.0 + 0.1 * torch.randn(D)
+    proj_w = 0.05 * torch.randn(N, D)
+    proj_b = torch.randn(N)
+    wscale = 0.5 + torch.rand(N)
+    scale = 1.0 / math.sqrt(D)
+    out = mk._eager_tree_attn_rmsnorm_linear(q, k, v, mask, rms_w, proj_w, proj_b, wscale, scale, 1e-6)
+    out_bare = mk._eager_tree_attn_rmsnorm_linear(q, k, v, mask, None, proj_w, None, None, 0.3, 1e-5)
+    # bf16 operands (the reference widens everything to fp32 and rounds the result once)
+    qb, kb, vb = (t.to(torch.bfloat16) for t in (q, k, v))
+    wb = proj_w.to(torch.bfloat16)
+    out_b = mk._eager_tree_attn_rmsnorm_linear(qb, kb, vb, mask, rms_w, wb, proj_b, None, scale, 1e-6)
+    out_nan = mk._eager_tree_attn_rmsnorm_linear(q[:1], k[:1], v[:1], torch.zeros(L), rms_w, proj_w, proj_b,
+                                                 None, scale, 1e-6)
+    save("tree_attn_rmsnorm_linear.npz", q=f32(q), k=f32(k), v=f32(v), mask=f32(mask), rms_w=f32(rms_w),
+         proj_w=f32(proj_w), proj_b=f32(proj_b), wscale=f32(wscale), scale=np.float32(scale).reshape(1),
+         out=f32(out), out_bare=f32(out_bare), q_bits=bits16(qb), k_bits=bits16(kb), v_bits=bits16(vb),
+         w_bits=bits16(wb), out_b_bits=bits16(out_b), out_nan=f32(out_nan))
 
 
 if __name__ == "__main__":

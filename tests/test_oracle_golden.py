@@ -141,6 +141,25 @@ def test_tree_attention(golden):
                                g["oL"], rtol=1e-5, atol=1e-5)
 
 
+def test_tree_attn_rmsnorm_linear(golden):
+    g = golden("tree_attn_rmsnorm_linear.npz")
+    s = float(g["scale"][0])
+    o = O.tree_attn_rmsnorm_linear(g["q"], g["k"], g["v"], g["mask"], g["rms_w"], g["proj_w"], g["proj_b"],
+                                   g["wscale"], s, 1e-6)
+    np.testing.assert_allclose(o, g["out"], rtol=1e-4, atol=1e-4)
+    o = O.tree_attn_rmsnorm_linear(g["q"], g["k"], g["v"], g["mask"], None, g["proj_w"], None, None, 0.3, 1e-5)
+    np.testing.assert_allclose(o, g["out_bare"], rtol=1e-4, atol=1e-4)
+    # bf16 operands widened to fp32, result rounded once to bf16
+    qb, kb, vb, wb = (O.bf16_bits_to_f32(g[n]) for n in ("q_bits", "k_bits", "v_bits", "w_bits"))
+    o = O.tree_attn_rmsnorm_linear(qb, kb, vb, g["mask"], g["rms_w"], wb, g["proj_b"], None, s, 1e-6)
+    ref = O.bf16_bits_to_f32(g["out_b_bits"])
+    assert np.max(np.abs(O.round_to_bf16(o) - ref)) <= 2.0 ** -7 * np.max(np.abs(ref))
+    # every key masked: NaN rows, as the reference's softmax gives
+    o = O.tree_attn_rmsnorm_linear(g["q"][:1], g["k"][:1], g["v"][:1], np.zeros(g["mask"].shape, np.float32),
+                                   g["rms_w"], g["proj_w"], g["proj_b"], None, s, 1e-6)
+    assert np.isnan(g["out_nan"]).all() and np.isnan(o).all()
+
+
 def test_paged_attention(golden):
     g = golden("paged_attention.npz")
     ps = int(g["page_size"][0])
