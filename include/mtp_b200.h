@@ -192,6 +192,29 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
                              int64_t D, int64_t num_pages, int64_t page_size, float scale,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Bytes of workspace mtp_tree_attn_rmsnorm_linear needs (the normalised
+ * attention output, [B*H, D] in the GEMM operand dtype).  Under GEMM
+ * schedule 1 add mtp_gemm_streamk_bytes(B*H, N, D, operand dtype), where the
+ * operand dtype is q's when proj_w has q's 16-bit dtype, else f32. */
+size_t mtp_tree_attn_rmsnorm_linear_workspace(int64_t B, int64_t H, int64_t D, int q_dtype, int w_dtype);
+
+/* out[b,h,:] = rmsnorm(attn[b,h,:]) * rms_w @ (proj_w * wscale[:,None])^T + proj_bias,
+ * attn = single-query tree attention of q[b,h] over k/v[b,h,0:L] under the
+ * shared mask[L] (key j kept iff mask[j] > 0.5).  Replaces
+ * fused_tree_attn_rmsnorm_linear, mtp_kernels.py:1222-1250 (which runs the
+ * eager _eager_tree_attn_rmsnorm_linear, 881-905).  q [B,H,D], k/v
+ * [B,H,L,D] (qkv_dtype), mask [L] f32 (NULL keeps every key), rms_w [D] f32
+ * or NULL (ones), proj_w [N,D] (any dtype), proj_bias [N] or NULL, wscale
+ * [N] f32 or NULL, out [B,H,N] in qkv_dtype.  D <= 8192.  The attention and
+ * RMSNorm run on CUDA cores (HBM-bound); the projection is the GEMM of
+ * mtp_rmsnorm_linear (tensor cores when proj_w and q share a 16-bit dtype).
+ * A row with every key masked is NaN, as in the reference. */
+int mtp_tree_attn_rmsnorm_linear(const void* q, const void* k, const void* v, int qkv_dtype, const float* mask,
+                                 const float* rms_w, const void* proj_w, int w_dtype, const void* proj_bias,
+                                 int bias_dtype, const float* wscale, void* out, int64_t B, int64_t H, int64_t L,
+                                 int64_t D, int64_t N, float scale, float eps, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* verification (lm_head GEMM -> argmax -> acceptance)                        */
 /* ------------------------------------------------------------------------- */

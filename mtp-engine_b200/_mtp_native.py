@@ -44,6 +44,9 @@ SIGNATURES = {
     "mtp_tree_attention_paged_workspace": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64]),
     "mtp_tree_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64,
                                       _i64, _i64, _i64, _i64, _f, _vp, _sz, _vp]),
+    "mtp_tree_attn_rmsnorm_linear_workspace": (_sz, [_i64, _i64, _i64, _i, _i]),
+    "mtp_tree_attn_rmsnorm_linear": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _i, _vp, _vp, _i64, _i64,
+                                          _i64, _i64, _i64, _f, _f, _vp, _sz, _vp]),
     "mtp_verify_workspace": (_sz, [_i64]),
     "mtp_verify_workspace_init": (_i, [_vp, _sz, _vp]),
     "mtp_fused_verify": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
@@ -169,7 +172,7 @@ def drop_workspace(device: torch.device, name: str) -> None:
 # GEMM schedule (stream-K needs room in the workspace, see include/mtp_b200.h)
 # --------------------------------------------------------------------------- #
 STREAMK_TAIL = 16640  # MTP_STREAMK_TAIL_BYTES: counters + the final 256 bytes
-_GEMM_WS = ("rmsnorm_linear", "rmsnorm_linear_fp8")
+_GEMM_WS = ("rmsnorm_linear", "rmsnorm_linear_fp8", "tree_attn_rmsnorm_linear")
 
 
 def _rest_fill(device: torch.device):

@@ -20,6 +20,7 @@
 #include "mtp_gemm_sk.cuh"
 #include "mtp_gemm_tc.cuh"
 #include "mtp_rownorm.cuh"
+#include "mtp_rowattn.cuh"
 #include "mtp_verify.cuh"
 
 using namespace mtp;
@@ -412,6 +413,55 @@ int noalloc_scratch(unsigned char** out) {
   return MTP_OK;
 }
 
+// --------------------------------------------------------------- tree attn -> RMSNorm -> linear
+// The normalised attention output is the GEMM's A operand: in the weight's
+// 16-bit dtype when q has that same dtype (tensor cores), else fp32.
+int tarl_operand_dtype(int q_dtype, int w_dtype) {
+  return (is16bit(w_dtype) && w_dtype == q_dtype) ? q_dtype : MTP_DTYPE_F32;
+}
+
+size_t tarl_base_bytes(int64_t B, int64_t H, int64_t D, int q_dtype, int w_dtype) {
+  const int ao = tarl_operand_dtype(q_dtype, w_dtype);
+  return align256((size_t)B * H * D * (ao == MTP_DTYPE_F32 ? 4 : 2));
+}
+
+template <typename T, typename TO, int VEC>
+int launch_rowattn_inst(const void* q, const void* k, const void* v, const float* mask, const float* gamma,
+                        void* out, int64_t rows, int64_t L, int64_t D, float scale, float eps, cudaStream_t s) {
+  auto kern = rowattn::row_attn_norm_kernel<T, TO, VEC>;
+  const size_t smem = rowattn::smem_bytes(L, D, VEC);
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  static size_t attr[kMaxDevices] = {0};
+  if (smem > 48 * 1024 && attr[dev] < smem) {
+    MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr[dev] = smem;
+  }
+  kern<<<(unsigned)rows, rowattn::kThreads, smem, s>>>(static_cast<const T*>(q), static_cast<const T*>(k),
+                                                       static_cast<const T*>(v), mask, gamma, static_cast<TO*>(out),
+                                                       (int)L, (int)D, scale, eps);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+template <typename T>
+int launch_rowattn_t(bool vec, bool out_f32, const void* q, const void* k, const void* v, const float* mask,
+                     const float* gamma, void* out, int64_t rows, int64_t L, int64_t D, float scale, float eps,
+                     cudaStream_t s) {
+  constexpr int V = std::is_same<T, float>::value ? 4 : 8;
+  if constexpr (std::is_same<T, float>::value) {
+    if (vec) return launch_rowattn_inst<T, float, V>(q, k, v, mask, gamma, out, rows, L, D, scale, eps, s);
+    return launch_rowattn_inst<T, float, 1>(q, k, v, mask, gamma, out, rows, L, D, scale, eps, s);
+  } else {
+    if (out_f32) {
+      if (vec) return launch_rowattn_inst<T, float, V>(q, k, v, mask, gamma, out, rows, L, D, scale, eps, s);
+      return launch_rowattn_inst<T, float, 1>(q, k, v, mask, gamma, out, rows, L, D, scale, eps, s);
+    }
+    if (vec) return launch_rowattn_inst<T, T, V>(q, k, v, mask, gamma, out, rows, L, D, scale, eps, s);
+    return launch_rowattn_inst<T, T, 1>(q, k, v, mask, gamma, out, rows, L, D, scale, eps, s);
+  }
+}
+
 }  // namespace
 
 // =========================================================================
@@ -649,6 +699,50 @@ int mtp_rmsnorm_linear_fp8(const void* x, int x_dtype, const float* x_scale, con
   GemmEpilogue ep = store_epilogue(rowf, wscale, bias, bias_dtype, 1.0f, y, y_dtype, N);
   return launch_gemm(a, MTP_DTYPE_E4M3, weight, MTP_DTYPE_E4M3, M, N, K, ep, s,
                      static_cast<uint8_t*>(workspace) + need, workspace_bytes - need);
+}
+
+// ---------------------------------------------------------------- tree attn -> RMSNorm -> linear
+size_t mtp_tree_attn_rmsnorm_linear_workspace(int64_t B, int64_t H, int64_t D, int q_dtype, int w_dtype) {
+  if (B < 0 || H < 0 || D < 0 || !valid_dtype(q_dtype) || !valid_dtype(w_dtype)) return 0;
+  return tarl_base_bytes(B, H, D, q_dtype, w_dtype);
+}
+
+int mtp_tree_attn_rmsnorm_linear(const void* q, const void* k, const void* v, int qkv_dtype, const float* mask,
+                                 const float* rms_w, const void* proj_w, int w_dtype, const void* proj_bias,
+                                 int bias_dtype, const float* wscale, void* out, int64_t B, int64_t H, int64_t L,
+                                 int64_t D, int64_t N, float scale, float eps, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (B < 0 || H < 0 || L < 0 || D <= 0 || N < 0) return fail(MTP_ERR_SHAPE, "bad sizes");
+  if (D > rowattn::kMaxD) return fail(MTP_ERR_SHAPE, "D=%lld above %d", (long long)D, rowattn::kMaxD);
+  if (!valid_dtype(qkv_dtype) || qkv_dtype == MTP_DTYPE_E4M3 || !valid_dtype(w_dtype))
+    return fail(MTP_ERR_DTYPE, "unsupported dtype combination q=%d w=%d", qkv_dtype, w_dtype);
+  const int64_t rows = B * H;
+  if (rows == 0 || N == 0) return MTP_OK;
+  if (rows > INT32_MAX || N > 0xFFFFFFFFLL) return fail(MTP_ERR_SHAPE, "size out of range");
+  if (!q || !proj_w || !out || (L > 0 && (!k || !v))) return fail(MTP_ERR_ARG, "null tensor pointer");
+  const int ao = tarl_operand_dtype(qkv_dtype, w_dtype);
+  const int vec_w = qkv_dtype == MTP_DTYPE_F32 ? 4 : 8;
+  const bool vec = D % vec_w == 0 && aligned16(q) && aligned16(workspace) &&
+                   (L == 0 || (aligned16(k) && aligned16(v)));
+  const size_t smem = rowattn::smem_bytes(L, D, vec ? vec_w : 1);
+  if (smem > 227 * 1024) return fail(MTP_ERR_SHAPE, "L=%lld, D=%lld need too much shared memory", (long long)L,
+                                     (long long)D);
+  const size_t need = tarl_base_bytes(B, H, D, qkv_dtype, w_dtype);
+  if (!workspace || workspace_bytes < need) return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  cudaStream_t s = as_stream(stream);
+  void* a = workspace;  // normalised attention output [rows, D] in dtype ao
+  const bool out_f32 = ao == MTP_DTYPE_F32;
+  int st;
+  if (qkv_dtype == MTP_DTYPE_BF16)
+    st = launch_rowattn_t<__nv_bfloat16>(vec, out_f32, q, k, v, mask, rms_w, a, rows, L, D, scale, eps, s);
+  else if (qkv_dtype == MTP_DTYPE_F16)
+    st = launch_rowattn_t<__half>(vec, out_f32, q, k, v, mask, rms_w, a, rows, L, D, scale, eps, s);
+  else
+    st = launch_rowattn_t<float>(vec, true, q, k, v, mask, rms_w, a, rows, L, D, scale, eps, s);
+  if (st) return st;
+  GemmEpilogue ep = store_epilogue(nullptr, wscale, proj_bias, bias_dtype, 1.0f, out, qkv_dtype, N);
+  return launch_gemm(a, ao, proj_w, w_dtype, rows, N, D, ep, s, static_cast<uint8_t*>(workspace) + need,
+                     workspace_bytes - need);
 }
 
 // ---------------------------------------------------------------- attention

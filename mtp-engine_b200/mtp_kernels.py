@@ -258,6 +258,60 @@ def fused_tree_attention_paged(
     return out
 
 
+def fused_tree_attn_rmsnorm_linear(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor,
+    proj_w: torch.Tensor,
+    rms_w: Optional[torch.Tensor] = None,
+    proj_bias: Optional[torch.Tensor] = None,
+    wscale: Optional[torch.Tensor] = None,
+    scale: Optional[float] = None,
+    eps: float = 1e-6,
+) -> torch.Tensor:
+    """Tree attention -> RMSNorm -> linear in one call (mtp_kernels.py:1222-1250;
+    eager semantics _eager_tree_attn_rmsnorm_linear, 881-905).
+
+    q [B,H,D], k/v [B,H,L,D], mask [L] (key j kept iff mask[j] > 0.5, shared
+    by every b, h); proj_w [N,D]; rms_w [D], proj_bias [N], wscale [N]
+    optional.  Returns [B,H,N] in q.dtype.  The attention output is
+    normalised in fp32 (not rounded to q.dtype first, as in the reference)
+    and rounded once as the projection's operand; a row whose keys are all
+    masked is NaN."""
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    proj_w = proj_w.contiguous()
+    B, H, D = q.shape
+    L = k.shape[2]
+    N = proj_w.shape[0]
+    assert k.shape == (B, H, L, D) and v.shape == (B, H, L, D)
+    assert proj_w.shape == (N, D)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)  # mtp_kernels.py:1238-1239
+    dev = _N.require_cuda(q, k, v, mask, proj_w, rms_w, proj_bias, wscale)
+    mask = mask.contiguous().to(torch.float32)
+    assert mask.numel() == L
+    k, v = k.to(q.dtype), v.to(q.dtype)
+    if rms_w is not None:
+        rms_w = rms_w.contiguous().to(torch.float32)
+        assert rms_w.shape == (D,)
+    if wscale is not None:
+        wscale = wscale.contiguous().to(torch.float32)
+        assert wscale.numel() == N
+    if proj_bias is not None:
+        proj_bias = proj_bias.contiguous()
+        assert proj_bias.numel() == N
+    out = torch.empty((B, H, N), dtype=q.dtype, device=q.device)
+    Lib = _N.lib()
+    qc, wc = _N.dtype_code(q), _N.dtype_code(proj_w)
+    operand = qc if (wc == qc and wc in (_N.DT_BF16, _N.DT_F16)) else _N.DT_F32
+    ws = _N.gemm_workspace(dev, "tree_attn_rmsnorm_linear",
+                           Lib.mtp_tree_attn_rmsnorm_linear_workspace(B, H, D, qc, wc), B * H, N, D, operand)
+    _N.check(Lib.mtp_tree_attn_rmsnorm_linear(
+        _N.ptr(q), _N.ptr(k), _N.ptr(v), qc, _N.ptr(mask), _N.ptr(rms_w), _N.ptr(proj_w), wc,
+        _N.ptr(proj_bias), _N.dtype_code(proj_bias) if proj_bias is not None else 0, _N.ptr(wscale),
+        _N.ptr(out), B, H, L, D, N, float(scale), float(eps), _N.ptr(ws), ws.numel(), _N.stream_handle(dev)),
+        "fused_tree_attn_rmsnorm_linear")
+    return out
+
+
 # --------------------------------------------------------------------------- #
 # FP8 helpers and the packed scale layout (host-side preparation, torch ops)
 # --------------------------------------------------------------------------- #
@@ -343,6 +397,7 @@ __all__ = [
     "KernelTuningConfig", "TUNING", "MAX_FP8", "build_tuning_config",
     "fused_rmsnorm_linear", "fused_rmsnorm_linear_fp8",
     "fused_tree_attention", "fused_paged_attention", "fused_tree_attention_paged",
+    "fused_tree_attn_rmsnorm_linear",
     "quantize_fp8_e4m3", "quantize_fp8_rows", "dequantize_fp8", "pack_scales", "unpack_scale_tensor",
     "_HAS_TRITON",
 ]
