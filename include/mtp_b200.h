@@ -308,6 +308,17 @@ int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* 
  * to INT64_MIN.  epoch is a device uint64 that starts at 0 on every rank;
  * all ranks must make the same sequence of calls. */
 size_t mtp_verify_exchange_bytes(int64_t rows, int world);
+
+/* The host step after fused_multi_verify in generate_fused /
+ * generate_optimized (mtp_engine.py:1244-1258, 1326-1337), on the device so
+ * the loop needs no .item(): n = min_b accepted_n[b] (one rollback index per
+ * step); step_tokens[b, 0:width] = draft[b, 0:n] ++ corrected[b] when n < D
+ * (width n + 1), else draft[b, 0:D] (width D); info[0] = n, info[1] = width.
+ * draft [B,D], accepted_n/corrected [B] int32 (outputs of
+ * mtp_fused_multi_verify), step_tokens [B, ld] int32 with ld >= D + 1
+ * recommended (ld >= D accepted), info [2] int32.  One small launch. */
+int mtp_verify_step(const int32_t* draft, const int32_t* accepted_n, const int32_t* corrected, int64_t B, int64_t D,
+                    int32_t* step_tokens, int64_t ld, int32_t* info, void* stream);
 int mtp_verify_exchange_chain(int64_t* keys, const void* peer_bufs, int rank, int world, uint64_t* epoch,
                               const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected,
                               int64_t B, int64_t S, void* stream);

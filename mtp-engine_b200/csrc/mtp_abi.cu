@@ -1216,6 +1216,17 @@ int mtp_verify_shard_keys_ws(const void* hidden, int h_dtype, const void* weight
                      workspace ? workspace_bytes : 0);
 }
 
+int mtp_verify_step(const int32_t* draft, const int32_t* accepted_n, const int32_t* corrected, int64_t B, int64_t D,
+                    int32_t* step_tokens, int64_t ld, int32_t* info, void* stream) {
+  if (B < 0 || D < 0 || ld < D || D > INT32_MAX) return fail(MTP_ERR_SHAPE, "bad step sizes");
+  if (!accepted_n || !info || (B > 0 && !corrected) || (B > 0 && D > 0 && (!draft || !step_tokens)))
+    return fail(MTP_ERR_ARG, "null pointer");
+  if (B == 0) return MTP_OK;
+  verify_step_kernel<<<1, 256, 0, as_stream(stream)>>>(draft, accepted_n, corrected, B, D, step_tokens, ld, info);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
 size_t mtp_verify_exchange_bytes(int64_t rows, int world) {
   if (rows < 0 || world < 1) return 0;
   return (size_t)2 * world * rows * 8 + (size_t)2 * world * 8;

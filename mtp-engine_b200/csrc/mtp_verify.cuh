@@ -162,6 +162,35 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The host step that follows fused_multi_verify in generate_fused and
+// generate_optimized (mtp_engine.py:1244-1258, 1326-1337), on the device:
+// n = min over the batch of accepted_n (one shared rollback index per step);
+// the step's tokens are draft[:, :n] followed by corrected when some draft
+// was rejected (n < D), else all D drafts; info = {n, width}.  One block.
+__global__ void __launch_bounds__(256)
+    verify_step_kernel(const int32_t* draft, const int32_t* accepted_n, const int32_t* corrected, int64_t B,
+                       int64_t D, int32_t* step_tokens, int64_t ld, int32_t* info) {
+  __shared__ int red[8];
+  int m = INT32_MAX;
+  for (int64_t b = threadIdx.x; b < B; b += blockDim.x) m = min(m, accepted_n[b]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  int n = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) n = min(n, red[w]);
+  n = max(0, min(n, (int)D));
+  const int64_t width = n == D ? D : (int64_t)n + 1;
+  for (int64_t i = threadIdx.x; i < B * width; i += blockDim.x) {
+    const int64_t b = i / width, j = i - b * width;
+    step_tokens[b * ld + j] = j < n ? draft[b * D + j] : corrected[b];
+  }
+  if (threadIdx.x == 0) {
+    info[0] = n;
+    info[1] = (int32_t)width;
+  }
+}
+
 __global__ void keys_fill_kernel(long long* keys, int64_t n, unsigned int* counter) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) keys[i] = KEY_EMPTY;

@@ -89,4 +89,39 @@ def fused_multi_verify(
     return accept, accepted_n, corrected
 
 
-__all__ = ["fused_verify", "fused_multi_verify"]
+def verify_step(draft: torch.Tensor, accepted_n: torch.Tensor,
+                corrected: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The host step that follows fused_multi_verify in generate_fused /
+    generate_optimized (mtp_engine.py:1244-1258, 1326-1337), on the device.
+
+    n = accepted_n.min() (one rollback index for the batch); the step's new
+    tokens are draft[:, :n] followed by corrected when n < D, else draft.
+    Returns (step_tokens [B, D+1] int32, info [2] int32 = (n, width)); the new
+    tokens are step_tokens[:, :width].  Nothing is read back to the host, so
+    a loop can stay on the device (or read the 8 bytes of info once)."""
+    dev = _N.require_cuda(draft, accepted_n, corrected)
+    draft = draft.contiguous().to(torch.int32)
+    accepted_n = accepted_n.contiguous().to(torch.int32)
+    corrected = corrected.contiguous().to(torch.int32)
+    B, D = draft.shape
+    assert accepted_n.shape == (B,) and corrected.shape == (B,)
+    step_tokens = torch.empty((B, D + 1), dtype=torch.int32, device=draft.device)
+    info = torch.zeros(2, dtype=torch.int32, device=draft.device)
+    if B == 0:
+        return step_tokens, info
+    _N.check(_N.lib().mtp_verify_step(_N.ptr(draft), _N.ptr(accepted_n), _N.ptr(corrected), B, D,
+                                      _N.ptr(step_tokens), D + 1, _N.ptr(info), _N.stream_handle(dev)),
+             "verify_step")
+    return step_tokens, info
+
+
+def fused_multi_verify_step(hidden: torch.Tensor, weight: torch.Tensor, draft: torch.Tensor,
+                            bias: Optional[torch.Tensor] = None):
+    """fused_multi_verify followed by verify_step: (accept, accepted_n,
+    corrected, step_tokens, info), all on the device, two launches."""
+    accept, accepted_n, corrected = fused_multi_verify(hidden, weight, draft, bias)
+    step_tokens, info = verify_step(draft, accepted_n, corrected)
+    return accept, accepted_n, corrected, step_tokens, info
+
+
+__all__ = ["fused_verify", "fused_multi_verify", "verify_step", "fused_multi_verify_step"]

@@ -10,7 +10,10 @@ falls back to it.
 Parity pin: every function below is checked against golden vectors that were
 produced by running the reference's own eager functions
 (``tests/golden/make_golden.py`` imports the reference and writes
-``tests/golden/*.npz``; ``tests/test_oracle_golden.py`` compares).
+``tests/golden/*.npz``; ``tests/test_oracle_golden.py`` compares), except
+``verify_step``: the reference has that step only inline in its generate
+loops, so it is restated from both loops and the two restatements are
+checked against each other (``tests/test_verify_step.py``).
 
 All citations are ``file:line`` within the reference project.
 
@@ -439,6 +442,33 @@ def fused_multi_verify(hidden: np.ndarray, w: np.ndarray, bias: Optional[np.ndar
     assert S == draft.shape[1] + 1
     top = logits_f32(hidden, w, bias).argmax(axis=-1).astype(np.int32).reshape(B, S)
     return chain_accept(top, draft)
+
+
+def verify_step(draft: np.ndarray, accepted_n: np.ndarray, corrected: np.ndarray,
+                variant: str = "optimized") -> Tuple[np.ndarray, int]:
+    """The host step after fused_multi_verify, restated from the reference's
+    inline code (no function of its own there):
+    ``generate_optimized`` (mtp_engine.py:1326-1337): n = min(accepted_n);
+    n == depth -> draft; n == 0 -> corrected[:, None]; else
+    cat(draft[:, :n], corrected[:, None]).
+    ``generate_fused`` (mtp_engine.py:1244-1258): a_n = min(accepted_n);
+    has_reject = sum(accept) < depth * batch (equivalently a_n < depth);
+    cat(draft[:, :a_n], corrected[:, None]) if has_reject else draft.
+    Returns (new_tokens [B, width] int32, n)."""
+    draft = np.asarray(draft, dtype=np.int32)
+    B, depth = draft.shape
+    corr = np.asarray(corrected, dtype=np.int32)
+    n = int(np.asarray(accepted_n).min())
+    if variant == "optimized":
+        if n == depth:
+            return draft.copy(), n
+        if n == 0:
+            return corr[:, None].copy(), n
+        return np.concatenate([draft[:, :n], corr[:, None]], axis=1), n
+    has_reject = n < depth
+    if has_reject:
+        return np.concatenate([draft[:, :n], corr[:, None]], axis=1), n
+    return draft.copy(), n
 
 
 def top2_margin(hidden: np.ndarray, w: np.ndarray, bias: Optional[np.ndarray]) -> np.ndarray:
