@@ -215,6 +215,21 @@ int mtp_tree_attn_rmsnorm_linear(const void* q, const void* k, const void* v, in
                                  int64_t D, int64_t N, float scale, float eps, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* Batched PagedKVCache write (replaces the per-token
+ * PagedKVCache.write_inplace, mtp_engine.py:582-586, which reads every page
+ * id to the host).  For b < B, h < H, t < n (and t < count[b] when count is
+ * given): logical = start + t, page = page_table[b, logical],
+ * k_pages[page, b, h, logical % page_size, :] = src_k[b, h, node, :] with
+ * node = node_idx[b, t] (e.g. the accepted path of a draft tree; NULL: t);
+ * v likewise.  Pools [num_pages, B, H, page_size, D] in dtype; sources
+ * [B, H, src_len, D] in src_dtype (converted like .to(dtype)); page_table
+ * [B, table_stride] int32.  Rows whose page id or node index is out of range
+ * are skipped and recorded (MTP_ERR_DEVICE via mtp_device_status). */
+int mtp_paged_kv_write(void* k_pages, void* v_pages, int dtype, const int32_t* page_table, int64_t table_stride,
+                       int64_t num_pages, int64_t page_size, const void* src_k, const void* src_v, int src_dtype,
+                       int64_t src_len, const int32_t* node_idx, const int32_t* count, int64_t B, int64_t H,
+                       int64_t D, int64_t start, int64_t n, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* verification (lm_head GEMM -> argmax -> acceptance)                        */
 /* ------------------------------------------------------------------------- */

@@ -47,6 +47,8 @@ SIGNATURES = {
     "mtp_tree_attn_rmsnorm_linear_workspace": (_sz, [_i64, _i64, _i64, _i, _i]),
     "mtp_tree_attn_rmsnorm_linear": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _i, _vp, _vp, _i64, _i64,
                                           _i64, _i64, _i64, _f, _f, _vp, _sz, _vp]),
+    "mtp_paged_kv_write": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _vp, _vp, _i, _i64, _vp, _vp, _i64, _i64,
+                                _i64, _i64, _i64, _vp]),
     "mtp_verify_workspace": (_sz, [_i64]),
     "mtp_verify_workspace_init": (_i, [_vp, _sz, _vp]),
     "mtp_fused_verify": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),

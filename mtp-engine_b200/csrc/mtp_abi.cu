@@ -21,6 +21,7 @@
 #include "mtp_gemm_tc.cuh"
 #include "mtp_rownorm.cuh"
 #include "mtp_rowattn.cuh"
+#include "mtp_kvwrite.cuh"
 #include "mtp_verify.cuh"
 
 using namespace mtp;
@@ -743,6 +744,50 @@ int mtp_tree_attn_rmsnorm_linear(const void* q, const void* k, const void* v, in
   GemmEpilogue ep = store_epilogue(nullptr, wscale, proj_bias, bias_dtype, 1.0f, out, qkv_dtype, N);
   return launch_gemm(a, ao, proj_w, w_dtype, rows, N, D, ep, s, static_cast<uint8_t*>(workspace) + need,
                      workspace_bytes - need);
+}
+
+// ---------------------------------------------------------------- paged KV write
+int mtp_paged_kv_write(void* k_pages, void* v_pages, int dtype, const int32_t* page_table, int64_t table_stride,
+                       int64_t num_pages, int64_t page_size, const void* src_k, const void* src_v, int src_dtype,
+                       int64_t src_len, const int32_t* node_idx, const int32_t* count, int64_t B, int64_t H,
+                       int64_t D, int64_t start, int64_t n, void* stream) {
+  if (B < 0 || H < 0 || D <= 0 || n < 0 || src_len < 0 || page_size <= 0 || num_pages < 0 || start < 0)
+    return fail(MTP_ERR_SHAPE, "bad KV write sizes");
+  if (start + n > table_stride) return fail(MTP_ERR_SHAPE, "logical positions [%lld, %lld) beyond the page table",
+                                            (long long)start, (long long)(start + n));
+  if (!node_idx && n > src_len) return fail(MTP_ERR_SHAPE, "n=%lld rows but the source holds %lld", (long long)n,
+                                            (long long)src_len);
+  if (!valid_dtype(dtype) || dtype == MTP_DTYPE_E4M3 || !valid_dtype(src_dtype) || src_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtypes pool=%d source=%d", dtype, src_dtype);
+  const int64_t rows = B * H * n;
+  if (rows == 0) return MTP_OK;
+  if (!k_pages || !v_pages || !page_table || !src_k || !src_v) return fail(MTP_ERR_ARG, "null tensor pointer");
+  if ((rows + 7) / 8 > INT32_MAX) return fail(MTP_ERR_SHAPE, "too many rows");
+  KvWriteArgs a{};
+  a.k_pages = k_pages;
+  a.v_pages = v_pages;
+  a.dtype = dtype;
+  a.page_table = page_table;
+  a.table_stride = table_stride;
+  a.num_pages = num_pages;
+  a.page_size = page_size;
+  a.src_k = src_k;
+  a.src_v = src_v;
+  a.src_dtype = src_dtype;
+  a.src_len = src_len;
+  a.node_idx = node_idx;
+  a.count = count;
+  a.B = B;
+  a.H = H;
+  a.D = D;
+  a.start = start;
+  a.n = n;
+  const int eb = dtype == MTP_DTYPE_F32 ? 4 : 2;
+  a.vec = src_dtype == dtype && (D * eb) % 16 == 0 && aligned16(k_pages) && aligned16(v_pages) &&
+          aligned16(src_k) && aligned16(src_v);
+  paged_kv_write_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, as_stream(stream)>>>(a);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
 }
 
 // ---------------------------------------------------------------- attention

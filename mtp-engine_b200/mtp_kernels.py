@@ -312,6 +312,44 @@ def fused_tree_attn_rmsnorm_linear(
     return out
 
 
+def paged_kv_write(
+    k_pages: torch.Tensor, v_pages: torch.Tensor, page_table: torch.Tensor, start: int,
+    k_new: torch.Tensor, v_new: torch.Tensor,
+    node_idx: Optional[torch.Tensor] = None, count: Optional[torch.Tensor] = None,
+) -> None:
+    """Write new K/V rows into a PagedKVCache pool in one launch (the batched
+    form of PagedKVCache.write_inplace, mtp_engine.py:582-586, without its
+    per-token .item()).
+
+    k_pages/v_pages [P,B,H,page_size,D] (written in place, must be
+    contiguous); page_table [B, L] int32 (PagedKVCache.page_table);
+    k_new/v_new [B,H,src_len,D]; row t of sequence b goes to logical position
+    start + t and comes from source row node_idx[b, t] ([B, n], e.g. the
+    accepted path of a draft tree) or t; count [B] (e.g. accepted_n + 1)
+    limits how many rows each sequence writes."""
+    assert k_pages.is_contiguous() and v_pages.is_contiguous(), "page pools are written in place"
+    P, B, H, page_size, D = k_pages.shape
+    assert v_pages.shape == k_pages.shape and v_pages.dtype == k_pages.dtype
+    page_table = page_table.contiguous().to(torch.int32)
+    k_new, v_new = k_new.contiguous(), v_new.to(k_new.dtype).contiguous()
+    assert k_new.shape[:2] == (B, H) and k_new.shape[3] == D and v_new.shape == k_new.shape
+    src_len = k_new.shape[2]
+    if node_idx is not None:
+        node_idx = node_idx.contiguous().to(torch.int32)
+        assert node_idx.dim() == 2 and node_idx.shape[0] == B
+        n = node_idx.shape[1]
+    else:
+        n = src_len
+    if count is not None:
+        count = count.contiguous().to(torch.int32)
+        assert count.shape == (B,)
+    dev = _N.require_cuda(k_pages, v_pages, page_table, k_new, v_new, node_idx, count)
+    _N.check(_N.lib().mtp_paged_kv_write(
+        _N.ptr(k_pages), _N.ptr(v_pages), _N.dtype_code(k_pages), _N.ptr(page_table), page_table.shape[-1], P,
+        page_size, _N.ptr(k_new), _N.ptr(v_new), _N.dtype_code(k_new), src_len, _N.ptr(node_idx), _N.ptr(count),
+        B, H, D, int(start), n, _N.stream_handle(dev)), "paged_kv_write")
+
+
 # --------------------------------------------------------------------------- #
 # FP8 helpers and the packed scale layout (host-side preparation, torch ops)
 # --------------------------------------------------------------------------- #
@@ -397,7 +435,7 @@ __all__ = [
     "KernelTuningConfig", "TUNING", "MAX_FP8", "build_tuning_config",
     "fused_rmsnorm_linear", "fused_rmsnorm_linear_fp8",
     "fused_tree_attention", "fused_paged_attention", "fused_tree_attention_paged",
-    "fused_tree_attn_rmsnorm_linear",
+    "fused_tree_attn_rmsnorm_linear", "paged_kv_write",
     "quantize_fp8_e4m3", "quantize_fp8_rows", "dequantize_fp8", "pack_scales", "unpack_scale_tensor",
     "_HAS_TRITON",
 ]

@@ -284,6 +284,29 @@ def paged_attention(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray,
     return tree_attention(q, k, v, np.ones(L, dtype=np.float32), scale)
 
 
+def paged_kv_write(k_pages: np.ndarray, v_pages: np.ndarray, page_table: np.ndarray, start: int,
+                   k_new: np.ndarray, v_new: np.ndarray, node_idx: Optional[np.ndarray] = None,
+                   count: Optional[np.ndarray] = None) -> Tuple[np.ndarray, np.ndarray]:
+    """Batched ``PagedKVCache.write_inplace``, mtp_engine.py:582-586: for each
+    token t, sequence b and head h, pid = page_table[b, start + t],
+    slot = (start + t) % page_size, pages[pid, b, h, slot] = new[b, h, node].
+    node = node_idx[b, t] or t; count[b] limits the tokens of sequence b.
+    Returns updated copies (values converted to the pool dtype by the caller)."""
+    kp, vp = np.array(k_pages, copy=True), np.array(v_pages, copy=True)
+    P, B, H, ps, D = kp.shape
+    n = node_idx.shape[1] if node_idx is not None else k_new.shape[2]
+    for b in range(B):
+        nb = n if count is None else min(n, int(count[b]))
+        for t in range(nb):
+            logical = start + t
+            pid = int(page_table[b, logical])
+            node = int(node_idx[b, t]) if node_idx is not None else t
+            for h in range(H):
+                kp[pid, b, h, logical % ps] = k_new[b, h, node]
+                vp[pid, b, h, logical % ps] = v_new[b, h, node]
+    return kp, vp
+
+
 def tree_attention_paged(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray,
                          page_table: np.ndarray, ctx_len: int, page_size: int,
                          tree_k: np.ndarray, tree_v: np.ndarray, tree_mask: np.ndarray,

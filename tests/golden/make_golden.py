@@ -69,6 +69,10 @@ def main():
     if args.only == "tree_attn_rmsnorm_linear":
         make_tree_attn_rmsnorm_linear(torch, mk)
         return
+    if args.only == "paged_kv_write":
+        import mtp_engine
+        make_paged_kv_write(torch, mtp_engine)
+        return
 
     # ---------------------------------------------------------------- rmsnorm_linear fp32
     torch.manual_seed(1)  # test_engine.py:5
@@ -272,6 +276,39 @@ def main():
     save("draft_tree.npz", **arrs)
 
     make_tree_attn_rmsnorm_linear(torch, mk)
+    import mtp_engine
+    make_paged_kv_write(torch, mtp_engine)
+
+
+def make_paged_kv_write(torch, mtp_engine):
+    """The reference's own PagedKVCache (mtp_engine.py:523-610) on the CPU:
+    reserve() builds the page table, write_inplace() (582-586) writes one
+    token of one head at a time.  A float32 pool and a bf16 pool written
+    from float32 rows (write_inplace casts with .to(self.dtype))."""
+    torch.manual_seed(22)
+    B, H, D, P, ps = 2, 3, 16, 8, 4
+    out = {}
+    for name, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+        kv = mtp_engine.PagedKVCache(batch=B, num_heads=H, head_dim=D, num_pages=P, page_size=ps,
+                                     device=torch.device("cpu"), dtype=dt)
+        kv.k_pages.normal_()
+        kv.v_pages.normal_()
+        before_k, before_v = kv.k_pages.clone(), kv.v_pages.clone()
+        start = kv.reserve(3)   # positions 0..2 (not written)
+        start = kv.reserve(9)   # positions 3..11 -> written below
+        n = 9
+        k_new = torch.randn(B, H, n, D)
+        v_new = torch.randn(B, H, n, D)
+        for t in range(n):
+            for b in range(B):
+                for h in range(H):
+                    kv.write_inplace(start + t, b, h, k_new[b, h, t], v_new[b, h, t])
+        conv = (lambda t_: f32(t_)) if dt == torch.float32 else (lambda t_: bits16(t_))
+        out.update({f"{name}_k_before": conv(before_k), f"{name}_v_before": conv(before_v),
+                    f"{name}_k_after": conv(kv.k_pages), f"{name}_v_after": conv(kv.v_pages),
+                    f"{name}_page_table": kv.page_table.numpy(), f"{name}_k_new": f32(k_new),
+                    f"{name}_v_new": f32(v_new), f"{name}_start": np.array([start], np.int64)})
+    save("paged_kv_write.npz", **out)
 
 
 def make_tree_attn_rmsnorm_linear(torch, mk):
