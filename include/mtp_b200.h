@@ -161,6 +161,26 @@ int mtp_tree_attention(const void* q, const void* k, const void* v, const float*
                        int dtype, int64_t B, int64_t H, int64_t L, int64_t D, float scale,
                        void* stream);
 
+/* Single-query attention per (b, h) over L contiguous keys, no mask, with K
+ * and V in kv_dtype (any, e.g. E4M3) scaled per head: k * kscale[h],
+ * v * vscale[h] (NULL = 1).  Replaces fused_causal_attention_fp8,
+ * mtp_kernels.py:1105-1133 (eager _eager_causal_attention_fp8, 817-830),
+ * and with kv_dtype = q_dtype and NULL scales fused_causal_attention,
+ * 980-1006 (eager 790-802).  q/out [B,H,D] in q_dtype, k/v [B,H,L,D],
+ * D <= 256. */
+int mtp_causal_attention_scaled(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype,
+                                const float* kscale, const float* vscale, void* out, int64_t B, int64_t H, int64_t L,
+                                int64_t D, float scale, void* stream);
+
+/* y[M,N] = x[M,K] @ dequant(packed, scales)^T with 4-bit weights packed two
+ * per byte along K (low nibble first) and decoded as (code - 8) *
+ * scales[n, k / group].  Replaces fused_int4_matmul, mtp_kernels.py:1194-1219
+ * (eager _eager_int4_matmul 875-878 over dequantize_int4 754-767).  packed
+ * [N, K/2] uint8, scales [N, ceil(K/group)] f32, K even; fp32 products and
+ * sums (the reference's fp32 dot). */
+int mtp_int4_matmul(const void* x, int x_dtype, const uint8_t* packed, const float* scales, int64_t group, void* y,
+                    int y_dtype, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* Single-query attention over a page pool with a per-token page table.
  * Replaces fused_paged_attention, mtp_kernels.py:1136-1162 (eager
  * _eager_paged_attention, 832-856).  k_pages/v_pages:

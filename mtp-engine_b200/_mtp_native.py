@@ -41,6 +41,8 @@ SIGNATURES = {
                                     _vp, _sz, _vp]),
     "mtp_tree_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _f, _vp]),
     "mtp_paged_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _f, _vp]),
+    "mtp_causal_attention_scaled": (_i, [_vp, _i, _vp, _vp, _i, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _vp]),
+    "mtp_int4_matmul": (_i, [_vp, _i, _vp, _vp, _i64, _vp, _i, _i64, _i64, _i64, _vp]),
     "mtp_tree_attention_paged_workspace": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64]),
     "mtp_tree_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64,
                                       _i64, _i64, _i64, _i64, _f, _vp, _sz, _vp]),

@@ -22,6 +22,7 @@
 #include "mtp_rownorm.cuh"
 #include "mtp_rowattn.cuh"
 #include "mtp_kvwrite.cuh"
+#include "mtp_int4.cuh"
 #include "mtp_verify.cuh"
 
 using namespace mtp;
@@ -823,6 +824,53 @@ int mtp_tree_attention(const void* q, const void* k, const void* v, const float*
   a.mask = mask;
   a.L = L;
   return launch_decode_attention(a, as_stream(stream));
+}
+
+int mtp_causal_attention_scaled(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype,
+                                const float* kscale, const float* vscale, void* out, int64_t B, int64_t H, int64_t L,
+                                int64_t D, float scale, void* stream) {
+  if (B < 0 || H < 0 || L < 0 || D <= 0) return fail(MTP_ERR_SHAPE, "bad attention sizes");
+  if (!valid_dtype(q_dtype) || q_dtype == MTP_DTYPE_E4M3 || !valid_dtype(kv_dtype))
+    return fail(MTP_ERR_DTYPE, "unsupported dtypes q=%d kv=%d", q_dtype, kv_dtype);
+  if (B * H == 0) return MTP_OK;
+  if (!q || !out || (L > 0 && (!k || !v))) return fail(MTP_ERR_ARG, "null tensor pointer");
+  AttnArgs a{};
+  a.kind = ATTN_CONTIG;
+  a.dtype = q_dtype;
+  a.q = q;
+  a.out = out;
+  a.B = B;
+  a.T = 1;
+  a.Hq = H;
+  a.Hkv = H;
+  a.D = D;
+  a.scale = scale;
+  a.k = k;
+  a.v = v;
+  a.mask = nullptr;
+  a.L = L;
+  a.kv_custom = 1;
+  a.kv_dtype = kv_dtype;
+  a.kscale = kscale;
+  a.vscale = vscale;
+  return launch_decode_attention(a, as_stream(stream));
+}
+
+int mtp_int4_matmul(const void* x, int x_dtype, const uint8_t* packed, const float* scales, int64_t group, void* y,
+                    int y_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
+  if (int st = check_dims(M, N, K)) return st;
+  if (K % 2 != 0) return fail(MTP_ERR_SHAPE, "K=%lld must be even (two codes per byte)", (long long)K);
+  if (group <= 0) return fail(MTP_ERR_SHAPE, "group must be positive");
+  if (!valid_dtype(x_dtype) || x_dtype == MTP_DTYPE_E4M3 || !valid_dtype(y_dtype) || y_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "unsupported dtypes x=%d y=%d", x_dtype, y_dtype);
+  if (M == 0 || N == 0) return MTP_OK;
+  if (!x || !packed || !scales || !y) return fail(MTP_ERR_ARG, "null tensor pointer");
+  if (M > 65535LL * w4::kTile || N > INT32_MAX / 2) return fail(MTP_ERR_SHAPE, "size out of range");
+  dim3 grid((unsigned)((N + w4::kTile - 1) / w4::kTile), (unsigned)((M + w4::kTile - 1) / w4::kTile));
+  w4::int4_matmul_kernel<<<grid, 256, 0, as_stream(stream)>>>(x, x_dtype, packed, scales, (int)group, y, y_dtype,
+                                                                 (int)M, (int)N, (int)K);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
 }
 
 int mtp_paged_attention(const void* q, const void* k_pages, const void* v_pages, const int32_t* page_table,

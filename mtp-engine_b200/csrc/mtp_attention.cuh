@@ -39,6 +39,13 @@ struct AttnArgs {
   const void* tree_k;
   const void* tree_v;
   const float* tree_mask;
+  // kv_custom != 0: K/V in kv_dtype (e.g. E4M3), each multiplied by
+  // kscale[kv head] / vscale[kv head] (null = 1) -- fused_causal_attention_fp8,
+  // mtp_kernels.py:1105-1133 (eager 817-830).  0: K/V in dtype, unscaled.
+  int kv_custom;
+  int kv_dtype;
+  const float* kscale;
+  const float* vscale;
 };
 
 constexpr int kAttnMaxDPerLane = 8;  // head_dim <= 256
@@ -55,6 +62,9 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(AttnArgs a) {
   const int64_t hk = h / (a.Hq / a.Hkv);
   const int64_t D = a.D;
   const int nd = (int)((D + 31) / 32);
+  const int kvdt = a.kv_custom ? a.kv_dtype : a.dtype;
+  const float ks = (a.kv_custom && a.kscale) ? a.kscale[hk] : 1.0f;
+  const float vs = (a.kv_custom && a.vscale) ? a.vscale[hk] : 1.0f;
 
   float qv[kAttnMaxDPerLane], acc[kAttnMaxDPerLane];
 #pragma unroll
@@ -99,7 +109,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(AttnArgs a) {
 #pragma unroll
     for (int i = 0; i < kAttnMaxDPerLane; ++i) {
       const int64_t d = lane + 32 * i;
-      if (i < nd && d < D) s = fmaf(qv[i], load_f32(kp, a.dtype, off + d), s);
+      if (i < nd && d < D) s = fmaf(qv[i], load_f32(kp, kvdt, off + d) * ks, s);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -111,7 +121,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(AttnArgs a) {
 #pragma unroll
     for (int i = 0; i < kAttnMaxDPerLane; ++i) {
       const int64_t d = lane + 32 * i;
-      if (i < nd && d < D) acc[i] = acc[i] * corr + p * load_f32(vp, a.dtype, off + d);
+      if (i < nd && d < D) acc[i] = acc[i] * corr + p * (load_f32(vp, kvdt, off + d) * vs);
     }
     m = m_new;
   }

@@ -190,6 +190,44 @@ def fused_tree_attention(
     return out
 
 
+def fused_causal_attention(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,
+) -> torch.Tensor:
+    """Single-query attention per (b, h) over all L keys (mtp_kernels.py:980-1006;
+    eager 790-802).  q [B,H,D], k/v [B,H,L,D] -> [B,H,D] in q.dtype."""
+    return _scaled_attention(q, k, v, None, None, scale, "fused_causal_attention")
+
+
+def fused_causal_attention_fp8(
+    q: torch.Tensor, k_fp8: torch.Tensor, v_fp8: torch.Tensor,
+    kscale: torch.Tensor, vscale: torch.Tensor, scale: Optional[float] = None,
+) -> torch.Tensor:
+    """Single-query attention with an FP8 (or any-dtype) KV cache scaled per
+    head: k = k_fp8 * kscale[h], v = v_fp8 * vscale[h] (mtp_kernels.py:1105-1133;
+    eager 817-830).  q [B,H,D], k_fp8/v_fp8 [B,H,L,D], kscale/vscale [H]."""
+    return _scaled_attention(q, k_fp8, v_fp8, kscale, vscale, scale, "fused_causal_attention_fp8")
+
+
+def _scaled_attention(q, k, v, kscale, vscale, scale, what):
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, D = q.shape
+    _B, _H, L, _D = k.shape
+    assert (B, H, D) == (_B, _H, _D) and v.shape == k.shape  # mtp_kernels.py:1116
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = _N.require_cuda(q, k, v, kscale, vscale)
+    v = v.to(k.dtype)
+    if kscale is not None:
+        kscale = kscale.contiguous().to(torch.float32)
+        vscale = vscale.contiguous().to(torch.float32)
+        assert kscale.numel() == H and vscale.numel() == H
+    out = torch.empty_like(q)
+    _N.check(_N.lib().mtp_causal_attention_scaled(
+        _N.ptr(q), _N.dtype_code(q), _N.ptr(k), _N.ptr(v), _N.dtype_code(k), _N.ptr(kscale), _N.ptr(vscale),
+        _N.ptr(out), B, H, L, D, float(scale), _N.stream_handle(dev)), what)
+    return out
+
+
 def fused_paged_attention(
     q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
     page_table: torch.Tensor, page_size: int, scale: Optional[float] = None,
@@ -350,6 +388,58 @@ def paged_kv_write(
         B, H, D, int(start), n, _N.stream_handle(dev)), "paged_kv_write")
 
 
+def fused_int4_matmul(
+    x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, K: int, group: int = 32,
+) -> torch.Tensor:
+    """y = x @ dequantize_int4(packed, scales, K, group)^T in one kernel
+    (mtp_kernels.py:1194-1219): x [M,K], packed [N,K/2] uint8 (two codes per
+    byte, low nibble first, decoded as code - 8), scales [N, ceil(K/group)].
+    Returns [M,N] in x.dtype; fp32 products and sums."""
+    x, packed, scales = x.contiguous(), packed.contiguous(), scales.contiguous().to(torch.float32)
+    M, _K = x.shape
+    assert _K == K  # mtp_kernels.py:1201
+    N = packed.shape[0]
+    assert packed.dtype == torch.uint8 and packed.shape == (N, K // 2)
+    assert scales.shape == (N, (K + group - 1) // group)
+    dev = _N.require_cuda(x, packed, scales)
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    _N.check(_N.lib().mtp_int4_matmul(_N.ptr(x), _N.dtype_code(x), _N.ptr(packed), _N.ptr(scales), int(group),
+                                      _N.ptr(y), _N.dtype_code(y), M, N, K, _N.stream_handle(dev)),
+             "fused_int4_matmul")
+    return y
+
+
+def quantize_int4(x: torch.Tensor, group: int = 32) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Group-wise 4-bit quantisation, as mtp_kernels.py:730-751 (host-side
+    preparation): per row and group of `group` columns s = amax / 7 (1 when
+    amax == 0), q = clamp(round(x / s), -8, 7), stored as the low nibble of
+    q's two's-complement byte, two per byte (low nibble first).  Note that
+    the reference decodes these nibbles as code - 8 (dequantize_int4), and so
+    does fused_int4_matmul."""
+    N, K = x.shape
+    xf = x.to(torch.float32)
+    G = (K + group - 1) // group
+    pad = G * group - K
+    xg = torch.nn.functional.pad(xf, (0, pad)).view(N, G, group)
+    amax = xg.abs().amax(dim=-1)
+    s = torch.where(amax > 0, amax / 7.0, torch.ones_like(amax))
+    q = torch.round(xg / s[..., None]).clamp(-8, 7).to(torch.int8).view(N, G * group)[:, :K]
+    nib = q.to(torch.int32) & 0x0F
+    if K % 2:
+        nib = torch.nn.functional.pad(nib, (0, 1))
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).to(torch.uint8)[:, : K // 2]
+    return packed.contiguous(), s.contiguous()
+
+
+def dequantize_int4(packed: torch.Tensor, scales: torch.Tensor, K: int, group: int) -> torch.Tensor:
+    """mtp_kernels.py:754-767: w[n, 2j] = (low nibble - 8), w[n, 2j+1] =
+    (high nibble - 8), times scales[n, k // group]; float32 [N, K]."""
+    b = packed.to(torch.int32)
+    w = torch.stack([(b & 0x0F) - 8, ((b >> 4) & 0x0F) - 8], dim=-1).view(packed.shape[0], -1)[:, :K]
+    g = torch.arange(K, device=packed.device) // group
+    return w.to(torch.float32) * scales.to(torch.float32)[:, g]
+
+
 # --------------------------------------------------------------------------- #
 # FP8 helpers and the packed scale layout (host-side preparation, torch ops)
 # --------------------------------------------------------------------------- #
@@ -436,6 +526,7 @@ __all__ = [
     "fused_rmsnorm_linear", "fused_rmsnorm_linear_fp8",
     "fused_tree_attention", "fused_paged_attention", "fused_tree_attention_paged",
     "fused_tree_attn_rmsnorm_linear", "paged_kv_write",
+    "fused_causal_attention", "fused_causal_attention_fp8", "fused_int4_matmul", "quantize_int4", "dequantize_int4",
     "quantize_fp8_e4m3", "quantize_fp8_rows", "dequantize_fp8", "pack_scales", "unpack_scale_tensor",
     "_HAS_TRITON",
 ]

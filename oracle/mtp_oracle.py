@@ -257,6 +257,56 @@ def tree_attn_rmsnorm_linear(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: 
     return out.astype(np.float32)
 
 
+def causal_attention_scaled(q: np.ndarray, k: np.ndarray, v: np.ndarray,
+                            kscale: Optional[np.ndarray], vscale: Optional[np.ndarray],
+                            scale: float) -> np.ndarray:
+    """``_eager_causal_attention_fp8``, mtp_kernels.py:817-830 (k * kscale[h],
+    v * vscale[h], every key kept); with no scales ``_eager_causal_attention``,
+    790-802.  k/v given as float32 values (decoded E4M3 for the fp8 cache).
+    Float32 result [B,H,D]."""
+    kf = np.asarray(k, dtype=np.float32)
+    vf = np.asarray(v, dtype=np.float32)
+    if kscale is not None:
+        kf = kf * np.asarray(kscale, dtype=np.float32)[None, :, None, None]
+        vf = vf * np.asarray(vscale, dtype=np.float32)[None, :, None, None]
+    return tree_attention(q, kf, vf, np.ones(kf.shape[2], np.float32), scale)
+
+
+def quantize_int4(x: np.ndarray, group: int = 32) -> Tuple[np.ndarray, np.ndarray]:
+    """mtp_kernels.py:730-751: per row and group s = amax / 7 (1 if amax == 0),
+    q = clamp(round_half_even(x / s), -8, 7), packed as the low nibble of q's
+    two's-complement byte, two per byte, low nibble first."""
+    xf = np.asarray(x, dtype=np.float32)
+    N, K = xf.shape
+    G = (K + group - 1) // group
+    scales = np.empty((N, G), np.float32)
+    q = np.empty((N, K), np.int32)
+    for g in range(G):
+        c0, c1 = g * group, min((g + 1) * group, K)
+        amax = np.abs(xf[:, c0:c1]).max(axis=1)
+        s = np.where(amax > 0, amax / np.float32(7.0), np.float32(1.0)).astype(np.float32)
+        scales[:, g] = s
+        q[:, c0:c1] = np.clip(np.round(xf[:, c0:c1] / s[:, None]), -8, 7).astype(np.int32)
+    nib = q & 0x0F
+    packed = (nib[:, 0:K - K % 2:2] | (nib[:, 1:K:2] << 4)).astype(np.uint8)
+    return packed, scales
+
+
+def dequantize_int4(packed: np.ndarray, scales: np.ndarray, K: int, group: int) -> np.ndarray:
+    """mtp_kernels.py:754-767: code - 8 from each nibble (low first), times
+    scales[n, k // group]; float32 [N, K]."""
+    b = np.asarray(packed, dtype=np.int32)
+    w = np.stack([(b & 0x0F) - 8, ((b >> 4) & 0x0F) - 8], axis=-1).reshape(b.shape[0], -1)[:, :K]
+    g = np.arange(K) // group
+    return w.astype(np.float32) * np.asarray(scales, dtype=np.float32)[:, g]
+
+
+def int4_matmul(x: np.ndarray, packed: np.ndarray, scales: np.ndarray, K: int, group: int) -> np.ndarray:
+    """``_eager_int4_matmul``, mtp_kernels.py:875-878: linear(x, dequant(W)),
+    float32."""
+    return (np.asarray(x, dtype=np.float32) @ dequantize_int4(packed, scales, K, group).T).astype(np.float32)
+
+
 def gather_paged_kv(pages: np.ndarray, page_table: np.ndarray, page_size: int,
                     L: Optional[int] = None) -> np.ndarray:
     """Per-token page gather of ``_eager_paged_attention``, mtp_kernels.py:839-848.

@@ -69,6 +69,9 @@ def main():
     if args.only == "tree_attn_rmsnorm_linear":
         make_tree_attn_rmsnorm_linear(torch, mk)
         return
+    if args.only == "quant_attention_int4":
+        make_quant_attention_int4(torch, mk)
+        return
     if args.only == "paged_kv_write":
         import mtp_engine
         make_paged_kv_write(torch, mtp_engine)
@@ -278,6 +281,41 @@ def main():
     make_tree_attn_rmsnorm_linear(torch, mk)
     import mtp_engine
     make_paged_kv_write(torch, mtp_engine)
+    make_quant_attention_int4(torch, mk)
+
+
+def make_quant_attention_int4(torch, mk):
+    """fused_causal_attention_fp8 / fused_causal_attention / fused_int4_matmul
+    through their eager bodies (mtp_kernels.py:817-830, 790-802, 875-878) and
+    the int4 host helpers quantize_int4 / dequantize_int4 (730-767).  The fp8
+    case uses genuine float8_e4m3fn K/V with per-head scales != 1 (the
+    reference's own self-check, mtp_engine.py:1802-1809, uses fp32 K/V and
+    unit scales); the int4 case follows mtp_engine.py:1812-1818 plus a
+    partial last group."""
+    torch.manual_seed(23)
+    B, H, L, D = 2, 3, 40, 64
+    q = torch.randn(B, H, D)
+    kf = torch.randn(B, H, L, D) * 3
+    vf = torch.randn(B, H, L, D) * 3
+    ks = torch.tensor([0.5, 1.25, 2.0])
+    vs = torch.tensor([1.5, 0.75, 1.0])
+    k8, v8 = kf.clamp(-448, 448).to(torch.float8_e4m3fn), vf.clamp(-448, 448).to(torch.float8_e4m3fn)
+    att8 = mk._eager_causal_attention_fp8(q, k8, v8, ks, vs, 1.0 / math.sqrt(D))
+    att = mk._eager_causal_attention(q, kf, vf, 0.2)
+    W = torch.randn(48, 96) * 2
+    W[3, :32] = 0.0
+    pk, sc = mk.quantize_int4(W, group=32)
+    Wd = mk.dequantize_int4(pk, sc, 96, 32)
+    x = torch.randn(5, 96)
+    y = mk._eager_int4_matmul(x, pk, sc, 96, 32)
+    W2 = torch.randn(20, 40)
+    pk2, sc2 = mk.quantize_int4(W2, group=32)  # last group holds 8 columns
+    x2 = torch.randn(3, 40)
+    y2 = mk._eager_int4_matmul(x2, pk2, sc2, 40, 32)
+    save("quant_attention_int4.npz", q=f32(q), k_bits=bits8(k8), v_bits=bits8(v8), kscale=f32(ks),
+         vscale=f32(vs), att8=f32(att8), kf=f32(kf), vf=f32(vf), att=f32(att), w=f32(W),
+         packed=pk.numpy(), scales=f32(sc), w_deq=f32(Wd), x=f32(x), y=f32(y), w2=f32(W2), packed2=pk2.numpy(),
+         scales2=f32(sc2), x2=f32(x2), y2=f32(y2))
 
 
 def make_paged_kv_write(torch, mtp_engine):

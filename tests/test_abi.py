@@ -73,5 +73,5 @@ def test_cpu_tensors_rejected():
 def test_out_of_scope_names():
     import mtp_kernels
     with pytest.raises(AttributeError, match="not part of the B200 hot path"):
-        mtp_kernels.fused_int4_matmul  # noqa: B018
+        mtp_kernels.fused_causal_attention_autotuned  # noqa: B018
     assert mtp_kernels._HAS_TRITON is False
