@@ -866,9 +866,22 @@ int mtp_int4_matmul(const void* x, int x_dtype, const uint8_t* packed, const flo
   if (M == 0 || N == 0) return MTP_OK;
   if (!x || !packed || !scales || !y) return fail(MTP_ERR_ARG, "null tensor pointer");
   if (M > 65535LL * w4::kTile || N > INT32_MAX / 2) return fail(MTP_ERR_SHAPE, "size out of range");
+  cudaStream_t s = as_stream(stream);
+  if (M <= 8 && K % 32 == 0 && aligned16(packed)) {
+    const int mr = M == 1 ? 1 : (M == 2 ? 2 : (M <= 4 ? 4 : 8));
+    const int rows = w4::gemv_block_rows(mr);
+    const unsigned blocks = (unsigned)((N + rows - 1) / rows);
+    const int g = (int)group, m = (int)M, n = (int)N, k = (int)K;
+    if (mr == 1) w4::int4_gemv_kernel<1><<<blocks, 256, 0, s>>>(x, x_dtype, packed, scales, g, y, y_dtype, m, n, k);
+    else if (mr == 2) w4::int4_gemv_kernel<2><<<blocks, 256, 0, s>>>(x, x_dtype, packed, scales, g, y, y_dtype, m, n, k);
+    else if (mr == 4) w4::int4_gemv_kernel<4><<<blocks, 256, 0, s>>>(x, x_dtype, packed, scales, g, y, y_dtype, m, n, k);
+    else w4::int4_gemv_kernel<8><<<blocks, 256, 0, s>>>(x, x_dtype, packed, scales, g, y, y_dtype, m, n, k);
+    MTP_LAUNCH_CHECK();
+    return MTP_OK;
+  }
   dim3 grid((unsigned)((N + w4::kTile - 1) / w4::kTile), (unsigned)((M + w4::kTile - 1) / w4::kTile));
-  w4::int4_matmul_kernel<<<grid, 256, 0, as_stream(stream)>>>(x, x_dtype, packed, scales, (int)group, y, y_dtype,
-                                                                 (int)M, (int)N, (int)K);
+  w4::int4_matmul_kernel<<<grid, 256, 0, s>>>(x, x_dtype, packed, scales, (int)group, y, y_dtype, (int)M, (int)N,
+                                              (int)K);
   MTP_LAUNCH_CHECK();
   return MTP_OK;
 }

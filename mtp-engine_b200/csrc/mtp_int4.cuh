@@ -83,5 +83,86 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Decode-sized M (<= 8 rows): the packed weight is streamed at HBM speed.
+// 8 warps per block, gemv_rows_per_warp(MR) weight rows per warp (fewer as
+// MR grows, to keep the rows x MR accumulators in registers); each lane owns
+// 32 consecutive K codes (one 16-byte load per row and 1024-element chunk).  x is staged
+// per chunk in shared memory transposed within 32-element groups, so lane l
+// reading code j of its vector hits bank l.  Per-lane partial sums, then a
+// warp reduction.  Needs K % 32 == 0 and a 16-byte-aligned packed array.
+__host__ __device__ constexpr int gemv_rows_per_warp(int mr) { return mr <= 2 ? 8 : (mr == 4 ? 4 : 2); }
+__host__ __device__ constexpr int gemv_block_rows(int mr) { return 8 * gemv_rows_per_warp(mr); }
+constexpr int kGemvKC = 1024;
+
+template <int MR>
+__global__ void __launch_bounds__(256)
+    int4_gemv_kernel(const void* x, int x_dt, const uint8_t* __restrict__ packed, const float* __restrict__ scales,
+                     int group, void* y, int y_dt, int M, int N, int K) {
+  constexpr int kGemvRowsPerWarp = gemv_rows_per_warp(MR);
+  __shared__ float xs[MR][kGemvKC];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * gemv_block_rows(MR) + warp * kGemvRowsPerWarp;
+  const int64_t row_bytes = K / 2;
+  const int64_t groups = (K + group - 1) / group;
+  const bool one_scale = group % 32 == 0;  // a lane's 32 codes share one scale
+  float acc[kGemvRowsPerWarp][MR];
+#pragma unroll
+  for (int r = 0; r < kGemvRowsPerWarp; ++r)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[r][m] = 0.f;
+
+  for (int kc = 0; kc < K; kc += kGemvKC) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < MR * kGemvKC; i += 256) {
+      const int m = i / kGemvKC, kl = i % kGemvKC, k = kc + kl;
+      xs[m][(kl & 31) * 32 + (kl >> 5)] = (m < M && k < K) ? load_f32(x, x_dt, (int64_t)m * K + k) : 0.f;
+    }
+    __syncthreads();
+    const int kb = kc + lane * 32;  // this lane's codes kb .. kb + 31
+    if (kb >= K) continue;
+    // every row's 32 codes first (rows past N: code 8 everywhere, weight 0)
+    uint32_t wd[kGemvRowsPerWarp][4];
+    float s0[kGemvRowsPerWarp];
+    const float* srow[kGemvRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kGemvRowsPerWarp; ++r) {
+      const int n = n0 + r < N ? n0 + r : N - 1;
+      srow[r] = scales + (int64_t)n * groups;
+      uint4 u = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+      if (n0 + r < N) u = __ldg(reinterpret_cast<const uint4*>(packed + (int64_t)n * row_bytes + kb / 2));
+      wd[r][0] = u.x;
+      wd[r][1] = u.y;
+      wd[r][2] = u.z;
+      wd[r][3] = u.w;
+      s0[r] = one_scale ? srow[r][kb / group] : 0.f;
+    }
+    // then each x value once, against every row
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float xv[MR];
+#pragma unroll
+      for (int m = 0; m < MR; ++m) xv[m] = xs[m][j * 32 + lane];
+#pragma unroll
+      for (int r = 0; r < kGemvRowsPerWarp; ++r) {
+        const int code = (int)((wd[r][j >> 3] >> (4 * (j & 7))) & 0xFu);
+        const float w = (float)(code - 8) * (one_scale ? s0[r] : srow[r][(kb + j) / group]);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) acc[r][m] = fmaf(xv[m], w, acc[r][m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kGemvRowsPerWarp; ++r) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      float v = acc[r][m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      const int n = n0 + r;
+      if (lane == 0 && m < M && n < N) store_f32(y, y_dt, (int64_t)m * N + n, v);
+    }
+  }
+}
+
 }  // namespace w4
 }  // namespace mtp

@@ -85,8 +85,15 @@ def test_device_int4(mk, golden):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M,N,K,group,dt", [(1, 4096, 4096, 128, torch.bfloat16), (130, 300, 1000, 32, torch.float32),
-                                            (16, 14336, 4096, 64, torch.float16)])
+@pytest.mark.parametrize("M,N,K,group,dt", [
+    (1, 4096, 4096, 128, torch.bfloat16),   # decode-sized: streamed GEMV kernel, one row of x
+    (2, 1000, 1024, 32, torch.float32),
+    (3, 777, 2048, 16, torch.float32),      # group 16: a scale per code pair of groups
+    (5, 300, 4096, 64, torch.float16),
+    (8, 14336, 4096, 128, torch.bfloat16),
+    (130, 300, 1000, 32, torch.float32),    # tile kernel (K not a multiple of 32)
+    (16, 14336, 4096, 64, torch.float16),   # tile kernel
+])
 def test_device_int4_sizes(mk, M, N, K, group, dt):
     d = torch.device("cuda", 0)
     gen = torch.Generator(device=d).manual_seed(M + N)
