@@ -236,7 +236,9 @@ def run_ours(args):
     # eagerly unless --graph is given: a graph holding an NCCL call must be
     # released before destroy_process_group (see the teardown below), and on
     # 2-8 GPUs the replays saved only a few percent.
-    use_graphs = (world == 1 or args.graph) and not args.no_graph
+    # With the peer-memory exchange the verify holds no NCCL call, so its graph
+    # needs no special teardown: replay graphs on N > 1 too.
+    use_graphs = (world == 1 or args.graph or args.exchange == "p2p") and not args.no_graph
     launches0 = N.lib().mtp_launch_count()
     graphs = []  # the only owner of the graph objects
     if use_graphs:
