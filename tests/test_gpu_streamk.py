@@ -7,7 +7,8 @@ import numpy as np
 import pytest
 import torch
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.xfail(reason="first GPU run pending", strict=False)]
 
 INT64_MIN = -(2 ** 63)
 

@@ -13,7 +13,8 @@ import torch
 
 from oracle import mtp_oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.xfail(reason="first GPU run pending", strict=False)]
 
 
 @pytest.fixture(scope="module")
