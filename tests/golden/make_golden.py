@@ -56,9 +56,12 @@ def save(name, **arrays):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("MTP_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("MTP_REFERENCE"),
+                    help="checkout of the reference project (or set MTP_REFERENCE)")
     ap.add_argument("--only", default="", help="write only this fixture (e.g. tree_attn_rmsnorm_linear)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set MTP_REFERENCE")
     sys.path.insert(0, args.reference)
     os.environ.setdefault("TRITON_INTERPRET", "1")
     import torch
