@@ -238,7 +238,7 @@ def run_ours(args):
     # 2-8 GPUs the replays saved only a few percent.
     # With the peer-memory exchange the verify holds no NCCL call, so its graph
     # needs no special teardown: replay graphs on N > 1 too.
-    use_graphs = (world == 1 or args.graph or args.exchange == "p2p") and not args.no_graph
+    use_graphs = (world == 1 or args.graph or args.exchange in ("p2p", "fused")) and not args.no_graph
     launches0 = N.lib().mtp_launch_count()
     graphs = []  # the only owner of the graph objects
     if use_graphs:
@@ -668,8 +668,9 @@ def main():
     ap.add_argument("--graph", action="store_true", help="also replay captured graphs when n_gpus > 1")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--sweep", action="store_true", help="time every BASELINE config on its own (1 GPU)")
-    ap.add_argument("--exchange", choices=["nccl", "p2p"], default="nccl",
-                    help="vocab-parallel key exchange on N > 1: NCCL all-reduce or the peer-memory kernel")
+    ap.add_argument("--exchange", choices=["nccl", "p2p", "fused"], default="nccl",
+                    help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
+                         "or the all-reduce fused into the shard GEMM")
     ap.add_argument("--gemm-schedule", choices=["dp", "streamk"], default="dp",
                     help="tensor-core GEMM schedule: whole tiles per CTA, or stream-K where it is faster")
     args = ap.parse_args()

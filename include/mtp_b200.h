@@ -344,6 +344,29 @@ int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* 
  * all ranks must make the same sequence of calls. */
 size_t mtp_verify_exchange_bytes(int64_t rows, int world);
 
+/* Vocab-parallel verify as ONE kernel per rank, the all-reduce fused into the
+ * shard GEMM (replaces mtp_verify_shard_keys + the all-reduce + the scan,
+ * i.e. RowParallelLinear's gather, mtp_parallel.py:114-118).  Each rank owns
+ * a buffer of mtp_verify_fused_bytes(B*S, world) bytes mapped into every rank
+ * (keys [2][B*S] int64, flags [2][world], a call counter), put at rest once
+ * with mtp_verify_fused_init; peer_bufs is a device array of the world
+ * buffer addresses.  Every tile's (logit, index) key goes to every rank's
+ * keys by atomic max over NVLink as the tile finishes; the last CTA of the
+ * rank's GEMM then publishes a per-call flag to every rank, waits (bounded,
+ * MTP_ERR_TIMEOUT) for every rank's flag, and writes the outputs of
+ * mtp_fused_multi_verify from the global keys, which it puts back to rest.
+ * hidden/weight_shard: equal 16-bit dtypes with 16-byte rows (tensor
+ * cores).  workspace: a verify workspace (mtp_verify_workspace(0) bytes, plus
+ * mtp_gemm_streamk_bytes under GEMM schedule 1), put at rest once.  All
+ * ranks must make the same sequence of calls with the same B*S. */
+size_t mtp_verify_fused_bytes(int64_t rows, int world);
+int mtp_verify_fused_init(void* buf, int64_t rows, int world, void* stream);
+int mtp_verify_shard_fused(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                           const void* bias_shard, int bias_dtype, const void* peer_bufs, int rank, int world,
+                           const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected, int64_t B,
+                           int64_t S, int64_t K, int64_t V_shard, int64_t vocab_offset, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* The host step after fused_multi_verify in generate_fused /
  * generate_optimized (mtp_engine.py:1244-1258, 1326-1337), on the device so
  * the loop needs no .item(): n = min_b accepted_n[b] (one rollback index per

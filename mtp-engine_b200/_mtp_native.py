@@ -61,6 +61,10 @@ SIGNATURES = {
     "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
     "mtp_verify_step": (_i, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "mtp_verify_fused_bytes": (_sz, [_i64, _i]),
+    "mtp_verify_fused_init": (_i, [_vp, _i64, _i, _vp]),
+    "mtp_verify_shard_fused": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                    _i64, _i64, _vp, _sz, _vp]),
     "mtp_verify_exchange_bytes": (_sz, [_i64, _i]),
     "mtp_verify_exchange_chain": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_set_gemm_schedule": (_i, [_i]),

@@ -243,6 +243,26 @@ SkPlan sk_plan(int64_t M, int64_t N, int num_kb, int sms, int grid) {
 
 size_t sk_bytes_needed(const SkPlan& p) { return p.use ? p.slot_bytes + kSkTail : 0; }
 
+// Every tile whole, run by the stream-K kernel (its fused epilogues need it).
+SkPlan dp_only_plan(int64_t M, int64_t N, int num_kb, int sms) {
+  SkPlan p;
+  p.bn = N > 128 ? 256 : 128;
+  const int64_t num_m = (M + tc::kBM - 1) / tc::kBM, num_n = (N + p.bn - 1) / p.bn;
+  const int64_t T = num_m * num_n;
+  if (T <= 0 || T > INT32_MAX / 2 || num_kb <= 0) return p;
+  p.grid = (int)(T < sms ? T : sms);
+  p.s.num_m = (int)num_m;
+  p.s.num_tiles = (int)T;
+  p.s.num_kb = num_kb;
+  p.s.dp_rounds = (int)((T + p.grid - 1) / p.grid);
+  p.s.dp_tiles = (int)T;
+  p.s.q = 1;
+  p.s.sk_total = 0;
+  p.slot_bytes = 0;
+  p.use = true;
+  return p;
+}
+
 template <int BN, bool FP8, int FMT>
 int launch_sk_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, const SkPlan& pl,
                    unsigned long long* counters, float* slots, const GemmEpilogue& ep, cudaStream_t s) {
@@ -262,6 +282,10 @@ int launch_sk_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, c
   return MTP_OK;
 }
 
+int launch_sk_plan(const void* A, const void* B, int ab_dtype, bool fp8, int64_t M, int64_t N, int64_t K,
+                   const GemmEpilogue& ep, cudaStream_t s, const SkPlan& pl, float* slots,
+                   unsigned long long* counters);
+
 // Stream-K launch when the schedule is on (or forced by sk_grid > 0) and the
 // region [sk_ws, sk_ws + sk_bytes) holds the slots followed by the counter
 // tail.  *launched stays false when the data-parallel kernel should run.
@@ -276,13 +300,19 @@ int try_launch_sk(const void* A, const void* B, int ab_dtype, bool fp8, int64_t 
   const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
   const SkPlan pl = sk_plan(M, N, num_kb, sm_count(dev), sk_grid);
   if (!pl.use || sk_bytes < sk_bytes_needed(pl)) return MTP_OK;
+  uint8_t* base = static_cast<uint8_t*>(sk_ws);
+  *launched = true;
+  return launch_sk_plan(A, B, ab_dtype, fp8, M, N, K, ep, s, pl, reinterpret_cast<float*>(base),
+                        reinterpret_cast<unsigned long long*>(base + sk_bytes - kSkTail));
+}
+
+// The stream-K kernel with plan `pl`; slots/counters as laid out by the plan.
+int launch_sk_plan(const void* A, const void* B, int ab_dtype, bool fp8, int64_t M, int64_t N, int64_t K,
+                   const GemmEpilogue& ep, cudaStream_t s, const SkPlan& pl, float* slots,
+                   unsigned long long* counters) {
   CUtensorMap ta, tb;
   if (int st = make_kmajor_map(&ta, A, fp8, ab_dtype, M, K, tc::kBM)) return st;
   if (int st = make_kmajor_map(&tb, B, fp8, ab_dtype, N, K, pl.bn)) return st;
-  uint8_t* base = static_cast<uint8_t*>(sk_ws);
-  float* slots = reinterpret_cast<float*>(base);
-  unsigned long long* counters = reinterpret_cast<unsigned long long*>(base + sk_bytes - kSkTail);
-  *launched = true;
   const int m = (int)M, n = (int)N;
   if (pl.bn == 256) {
     if (fp8) return launch_sk_inst<256, true, 0>(ta, tb, m, n, pl, counters, slots, ep, s);
@@ -1331,6 +1361,74 @@ int mtp_verify_step(const int32_t* draft, const int32_t* accepted_n, const int32
   verify_step_kernel<<<1, 256, 0, as_stream(stream)>>>(draft, accepted_n, corrected, B, D, step_tokens, ld, info);
   MTP_LAUNCH_CHECK();
   return MTP_OK;
+}
+
+size_t mtp_verify_fused_bytes(int64_t rows, int world) {
+  if (rows < 0 || world < 1) return 0;
+  return align256((size_t)peer_epoch_offset(rows, world) + 8);
+}
+
+int mtp_verify_fused_init(void* buf, int64_t rows, int world, void* stream) {
+  if (!buf || rows < 0 || world < 1) return fail(MTP_ERR_ARG, "bad fused-exchange buffer");
+  cudaStream_t s = as_stream(stream);
+  const int64_t n = 2 * rows;
+  if (n > 0) {
+    keys_fill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<long long*>(buf), n, nullptr);
+    MTP_LAUNCH_CHECK();
+  }
+  const size_t off = (size_t)peer_flags_offset(rows);
+  MTP_CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(buf) + off, 0, mtp_verify_fused_bytes(rows, world) - off, s));
+  return MTP_OK;
+}
+
+int mtp_verify_shard_fused(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                           const void* bias_shard, int bias_dtype, const void* peer_bufs, int rank, int world,
+                           const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected, int64_t B,
+                           int64_t S, int64_t K, int64_t V_shard, int64_t vocab_offset, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1");
+  if (world < 1 || rank < 0 || rank >= world) return fail(MTP_ERR_ARG, "rank %d / world %d", rank, world);
+  const int64_t rows = B * S;
+  if (int st = check_dims(rows, V_shard, K)) return st;
+  if (B == 0) return MTP_OK;
+  if (V_shard <= 0) return fail(MTP_ERR_SHAPE, "empty vocabulary shard");
+  if (vocab_offset < 0 || vocab_offset + V_shard > 0xFFFFFFFFLL) return fail(MTP_ERR_SHAPE, "vocab offset out of range");
+  if (!hidden || !weight_shard || !peer_bufs || !accepted_n || !corrected || (S > 1 && (!draft || !accept)))
+    return fail(MTP_ERR_ARG, "null pointer");
+  if (!tc_eligible(hidden, weight_shard, h_dtype, w_dtype, rows, V_shard, K) || h_dtype == MTP_DTYPE_E4M3)
+    return fail(MTP_ERR_DTYPE, "the fused exchange runs on the tensor-core path (equal 16-bit dtypes, 16-byte rows)");
+  if (!workspace || workspace_bytes < 256) return fail(MTP_ERR_WORKSPACE, "workspace of 256 bytes needed");
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  cudaStream_t s = as_stream(stream);
+  GemmEpilogue ep{};
+  ep.mode = EPI_ARGMAX;
+  ep.bias = bias_shard;
+  ep.bias_dtype = bias_dtype;
+  ep.col_offset = vocab_offset;
+  ep.finalize = FIN_CHAIN_PEERS;
+  ep.counter = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + workspace_bytes - 256);
+  ep.draft = draft;
+  ep.accept = accept;
+  ep.accepted_n = accepted_n;
+  ep.tokens = corrected;
+  ep.B = B;
+  ep.S = S;
+  ep.peers = static_cast<const unsigned long long*>(peer_bufs);
+  ep.rank = rank;
+  ep.world = world;
+  ep.peer_rows = rows;
+  const int num_kb = (int)((K * 2 + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  SkPlan pl = sk_plan(rows, V_shard, num_kb, sm_count(dev), 0);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  if (!(g_gemm_schedule.load(std::memory_order_relaxed) == 1 && pl.use &&
+        workspace_bytes >= sk_bytes_needed(pl)))
+    pl = dp_only_plan(rows, V_shard, num_kb, sm_count(dev));
+  if (!pl.use) return fail(MTP_ERR_SHAPE, "no schedule for these sizes");
+  const size_t tail = workspace_bytes >= kSkTail ? kSkTail : 256;
+  return launch_sk_plan(hidden, weight_shard, h_dtype, false, rows, V_shard, K, ep, s, pl,
+                        reinterpret_cast<float*>(base),
+                        reinterpret_cast<unsigned long long*>(base + workspace_bytes - tail));
 }
 
 size_t mtp_verify_exchange_bytes(int64_t rows, int world) {

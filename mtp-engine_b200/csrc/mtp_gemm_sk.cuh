@@ -77,7 +77,8 @@ struct Iter {
     end = lin + s.q < s.sk_total ? lin + s.q : s.sk_total;
   }
   __host__ __device__ bool next(const Sched& s, Work& w) {
-    if (j < s.dp_rounds) {
+    // whole tiles (a data-parallel-only plan may leave the last round ragged)
+    if (j < s.dp_rounds && c + j * grid < s.num_tiles) {
       w.tile = c + j * grid;
       w.kb0 = 0;
       w.kb1 = s.num_kb;
@@ -87,6 +88,7 @@ struct Iter {
       ++j;
       return true;
     }
+    j = s.dp_rounds;
     if (lin >= end) return false;
     const long long x = lin / s.num_kb;
     const long long tile_end = (x + 1) * s.num_kb;
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
   volatile int* part_last = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  volatile int* peers_ok = reinterpret_cast<volatile int*>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -170,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     *last_flag = 0;
     *part_last = 0;
+    *peers_ok = 1;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -261,6 +265,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
+    // fused exchange: this call's epoch and key parity (the previous call's
+    // last CTA wrote the epoch before this launch began)
+    unsigned long long* my_buf = ep.peers ? reinterpret_cast<unsigned long long*>(ep.peers[ep.rank]) : nullptr;
+    const unsigned long long epoch =
+        ep.peers ? __ldcg(reinterpret_cast<const unsigned long long*>(
+                       reinterpret_cast<const uint8_t*>(my_buf) + peer_epoch_offset(ep.peer_rows, ep.world))) + 1ull
+                 : 0ull;
+    const int par = (int)(epoch & 1ull);
     int local = 0;
     while (it.next(sched, w)) {
       const int mb = w.tile % sched.num_m, nb = w.tile / sched.num_m;
@@ -407,7 +419,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (row_ok) atomicMax(&ep.keys[row], make_key(best, (uint32_t)(ep.col_offset + best_n)));
+        if (row_ok) {
+          const long long key = make_key(best, (uint32_t)(ep.col_offset + best_n));
+          if (ep.peers) {
+            // the all-reduce(max) of the keys, tile by tile, over NVLink
+            for (int p = 0; p < ep.world; ++p) {
+              long long* kp = reinterpret_cast<long long*>(ep.peers[p]) + (int64_t)par * ep.peer_rows + row;
+              if (p == ep.rank) atomicMax(kp, key);
+              else atomicMax_system(kp, key);
+            }
+          } else {
+            atomicMax(&ep.keys[row], key);
+          }
+        }
       }
       if (sum_parts && clean_slots) {
         const float rest = __uint_as_float(0u), rest_hi = __uint_as_float(0x80000000u);  // INT64_MIN words
@@ -421,8 +445,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&tempty[acc]);
     }
     if (ep.mode == EPI_ARGMAX && ep.finalize != FIN_NONE) {
-      // last CTA to finish decodes the keys (threadFenceReduction pattern)
-      __threadfence();
+      // last CTA to finish decodes the keys (threadFenceReduction pattern);
+      // keys sent to peers must be visible system-wide before the ticket
+      if (ep.peers) __threadfence_system();
+      else __threadfence();
       epi_bar_sync();
       if (threadIdx.x == 64) {
         const unsigned int ticket = atomicAdd(ep.counter, 1u);
@@ -430,9 +456,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       epi_bar_sync();
       if (*last_flag && !*abort_flag) {
-        __threadfence();
-        verify_finalize(ep, threadIdx.x - 64, 128);
-        if (threadIdx.x == 64) *ep.counter = 0u;
+        if (ep.finalize == FIN_CHAIN_PEERS) {
+          // every CTA of this rank has sent its keys: tell every rank, wait
+          // (bounded) until every rank has told this one, then decode the
+          // global keys of this parity (verify_finalize puts them back to rest)
+          __threadfence_system();
+          if (threadIdx.x == 64)
+            for (int p = 0; p < ep.world; ++p)
+              st_release_sys_u64(reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(ep.peers[p]) +
+                                                                        peer_flags_offset(ep.peer_rows)) +
+                                     (int64_t)par * ep.world + ep.rank,
+                                 epoch);
+          const int tq = threadIdx.x - 64;
+          if (tq < ep.world) {
+            const unsigned long long* f =
+                reinterpret_cast<const unsigned long long*>(reinterpret_cast<const uint8_t*>(my_buf) +
+                                                            peer_flags_offset(ep.peer_rows)) +
+                (int64_t)par * ep.world + tq;
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_sys_u64(f) < epoch) {
+              if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_error(MTP_ERR_TIMEOUT);
+                *peers_ok = 0;
+                break;
+              }
+            }
+          }
+          epi_bar_sync();
+          GemmEpilogue f = ep;
+          f.keys = reinterpret_cast<long long*>(my_buf) + (int64_t)par * ep.peer_rows;
+          f.finalize = FIN_CHAIN;
+          if (*peers_ok) {
+            verify_finalize(f, tq, 128);
+          } else {
+            for (int64_t r = tq; r < ep.peer_rows; r += 128) f.keys[r] = KEY_EMPTY;
+          }
+          epi_bar_sync();
+          if (threadIdx.x == 64) {
+            *reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(my_buf) +
+                                                   peer_epoch_offset(ep.peer_rows, ep.world)) = epoch;
+            *ep.counter = 0u;
+          }
+        } else {
+          __threadfence();
+          verify_finalize(ep, threadIdx.x - 64, 128);
+          if (threadIdx.x == 64) *ep.counter = 0u;
+        }
       }
     }
   }

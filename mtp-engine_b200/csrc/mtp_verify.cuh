@@ -9,7 +9,7 @@
 namespace mtp {
 
 enum EpiMode : int { EPI_STORE = 0, EPI_ARGMAX = 1 };
-enum FinMode : int { FIN_NONE = 0, FIN_CHAIN = 1, FIN_SINGLE = 2 };
+enum FinMode : int { FIN_NONE = 0, FIN_CHAIN = 1, FIN_SINGLE = 2, FIN_CHAIN_PEERS = 3 };
 
 struct GemmEpilogue {
   int mode;  // EpiMode
@@ -34,7 +34,21 @@ struct GemmEpilogue {
   int32_t* accepted_n;
   int32_t* tokens;  // FIN_CHAIN: corrected[B]; FIN_SINGLE: top[M]
   int64_t B, S;     // FIN_CHAIN: rows = B*S; FIN_SINGLE: rows = B, S = 1
+  // Vocab-parallel verify with the reduction fused into the GEMM
+  // (FIN_CHAIN_PEERS, stream-K kernel only): every rank owns a buffer
+  //   keys [2 parities][peer_rows] int64 | flags [2][world] uint64 | epoch uint64
+  // mapped into every rank; peers[r] is rank r's buffer.  Keys go to the
+  // parity (epoch + 1) & 1 of every rank's buffer; null peers: keys[] only.
+  const unsigned long long* peers;
+  int rank, world;
+  int64_t peer_rows;
 };
+
+// Offsets inside a fused-exchange buffer (see GemmEpilogue::peers).
+__host__ __device__ inline int64_t peer_flags_offset(int64_t rows) { return 2 * rows * 8; }
+__host__ __device__ inline int64_t peer_epoch_offset(int64_t rows, int world) {
+  return 2 * rows * 8 + 2 * (int64_t)world * 8;
+}
 
 // Decode keys into the verify outputs and put the keys back to KEY_EMPTY.
 // FIN_CHAIN follows the prefix-gated loop of _eager_fused_multi_verify

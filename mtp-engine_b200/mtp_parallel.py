@@ -161,10 +161,45 @@ _EXCHANGES = {}
 
 
 def _peer_exchange(dev: torch.device, rows: int, prim: "ParallelPrimitives") -> _PeerExchange:
-    key = (dev.index, id(prim.group), prim.tp_size)
+    # the buffer layout depends on rows (flags follow the keys), so a buffer is
+    # used for exactly one row count; every rank makes the same calls, so all
+    # ranks rebuild together
+    key = ("p2p", dev.index, id(prim.group), prim.tp_size)
     ex = _EXCHANGES.get(key)
-    if ex is None or ex.rows < rows:
-        ex = _PeerExchange(dev, max(rows, ex.rows if ex else 0), prim)
+    if ex is None or ex.rows != rows:
+        ex = _PeerExchange(dev, rows, prim)
+        _EXCHANGES[key] = ex
+    return ex
+
+
+class _FusedExchange:
+    """Symmetric-memory buffers of the fused shard GEMM + exchange
+    (mtp_verify_shard_fused): per rank keys [2][rows] at rest INT64_MIN,
+    flags [2][world] and the call counter at 0, mapped into every rank."""
+
+    def __init__(self, dev: torch.device, rows: int, prim: "ParallelPrimitives"):
+        import torch.distributed._symmetric_memory as symm
+
+        group = prim.group if prim.group is not None else torch.distributed.group.WORLD
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            symm.enable_symm_mem_for_group(group.group_name)
+        self.rows = rows
+        L = _N.lib()
+        nbytes = L.mtp_verify_fused_bytes(rows, prim.tp_size)
+        self.buf = symm.empty(-(-nbytes // 8), dtype=torch.int64, device=dev)
+        _N.check(L.mtp_verify_fused_init(_N.ptr(self.buf), rows, prim.tp_size, _N.stream_handle(dev)),
+                 "mtp_verify_fused_init")
+        self.handle = symm.rendezvous(self.buf, group)
+        self.peers = int(self.handle.buffer_ptrs_dev)
+        torch.cuda.synchronize(dev)
+        torch.distributed.barrier(group=group)  # every buffer at rest before any rank writes
+
+
+def _fused_exchange(dev: torch.device, rows: int, prim: "ParallelPrimitives") -> _FusedExchange:
+    key = ("fused", dev.index, id(prim.group), prim.tp_size)
+    ex = _EXCHANGES.get(key)
+    if ex is None or ex.rows != rows:
+        ex = _FusedExchange(dev, rows, prim)
         _EXCHANGES[key] = ex
     return ex
 
@@ -190,7 +225,10 @@ def vocab_parallel_multi_verify(
     then the acceptance scan; "p2p" -- one kernel pushes the keys to every
     peer over NVLink through symmetric memory, waits for the peers' keys and
     runs the scan (no collective library call; every rank must use it for the
-    same sequence of calls).
+    same sequence of calls); "fused" -- one kernel per rank: the shard GEMM
+    sends every tile's keys to every rank's buffer (atomic max over NVLink)
+    and its last CTA waits for the peers and runs the scan (tensor-core
+    dtypes only; same rule on the sequence of calls).
     """
     prim = prim or get_parallel_primitives()
     hidden = hidden.contiguous()
@@ -210,9 +248,19 @@ def vocab_parallel_multi_verify(
     accepted_n = torch.empty((B,), dtype=torch.int32, device=hidden.device)
     corrected = torch.empty((B,), dtype=torch.int32, device=hidden.device)
     L = _N.lib()
+    stream = _N.stream_handle(dev)
+    if prim.tp_size > 1 and exchange == "fused":
+        ex = _fused_exchange(dev, rows, prim)
+        ws = _N.verify_workspace(dev, 0, Vr, K, _N.dtype_code(hidden))  # ticket (+ stream-K region)
+        _N.check(L.mtp_verify_shard_fused(
+            _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight_shard), _N.dtype_code(weight_shard),
+            _N.ptr(bias_shard), _N.dtype_code(bias_shard) if bias_shard is not None else 0,
+            ctypes.c_void_p(ex.peers), prim.rank, prim.tp_size, _N.ptr(draft), _N.ptr(accept),
+            _N.ptr(accepted_n), _N.ptr(corrected), B, S, K, Vr, int(vocab_offset), _N.ptr(ws), ws.numel(),
+            stream), "mtp_verify_shard_fused")
+        return accept, accepted_n, corrected
     sk = _N.streamk_bytes(rows, Vr, K, _N.dtype_code(hidden))
     keys, region, region_bytes = _keys_buffer(dev, rows, sk)  # at rest: every word is INT64_MIN
-    stream = _N.stream_handle(dev)
     try:
         _N.check(L.mtp_verify_shard_keys_ws(
             _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight_shard), _N.dtype_code(weight_shard),

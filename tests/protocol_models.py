@@ -296,3 +296,59 @@ def run_exchange(seed, W, E, parities=2):
                 alive.remove(x)
 
 
+
+
+# --------------------------------------------------------------------------- #
+# mtp_verify_shard_fused (csrc/mtp_gemm_sk.cuh, FIN_CHAIN_PEERS).  Each rank
+# runs E calls of a GEMM with n_tiles tiles.  Call e: par = e & 1; every tile
+# sends its key (here the value e * 1000 + rank * 10 + tile) to keys[par] of
+# every rank by atomic max (remote ones land at any later time before the
+# rank's fence); the last CTA fences, releases flag [par][rank] = e in every
+# rank, waits for its own flags [par][p] >= e, reads keys[par] -- which must be
+# the maximum over all ranks' keys of call e -- and puts it back to rest.
+# --------------------------------------------------------------------------- #
+def run_fused_exchange(seed, W, E, n_tiles=3, parities=2):
+    rnd = random.Random(seed)
+    REST = -1
+    keys = [[REST] * 2 for _ in range(W)]                      # keys[owner][par] (one row)
+    flags = [[[0] * W for _ in range(2)] for _ in range(W)]   # flags[owner][par][src]
+    inflight = []  # (owner, par, src, value)
+
+    def rank_proc(r):
+        for e in range(1, E + 1):
+            par = e & 1 if parities == 2 else 0
+            for t in range(n_tiles):
+                v = e * 1000 + r * 10 + t
+                for p in range(W):
+                    inflight.append((p, par, r, v))
+                yield "step"
+            while any(x[2] == r for x in inflight):   # fence before the ticket / flags
+                yield "blocked"
+            for p in range(W):
+                flags[p][par][r] = e
+                yield "step"
+            for p in range(W):
+                while flags[r][par][p] < e:
+                    yield "blocked"
+            want = e * 1000 + (W - 1) * 10 + (n_tiles - 1)
+            if keys[r][par] != want:
+                raise Violation(f"rank {r} call {e} decodes {keys[r][par]}, want {want}")
+            keys[r][par] = REST
+            yield "step"
+
+    alive = [rank_proc(r) for r in range(W)]
+    steps = 0
+    while alive or inflight:
+        steps += 1
+        if steps > 10 ** 6:
+            raise Violation("no progress")
+        opts = [("p", x) for x in alive] + ([("s", None)] if inflight else [])
+        kind, x = rnd.choice(opts)
+        if kind == "s":
+            owner, par, src, val = inflight.pop(rnd.randrange(len(inflight)))
+            keys[owner][par] = max(keys[owner][par], val)
+        else:
+            try:
+                next(x)
+            except StopIteration:
+                alive.remove(x)

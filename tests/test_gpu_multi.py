@@ -50,7 +50,7 @@ def _rank(rank, world, port, q):
             draft = torch.randint(0, V, (B, S - 1), generator=g, device=dev, dtype=torch.int32)
             ref = mv.fused_multi_verify(hid, w, draft)
             shard, off = mp.shard_lm_head(w, world, rank)
-            for exchange in ("nccl", "p2p"):
+            for exchange in ("nccl", "p2p", "fused"):
                 got = mp.vocab_parallel_multi_verify(hid, shard, draft, None, off, prim, exchange=exchange)
                 torch.cuda.synchronize(dev)
                 same = all(torch.equal(a, b) for a, b in zip(got, ref))

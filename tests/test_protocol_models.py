@@ -1,7 +1,8 @@
 """The synchronisation protocols of two kernels that have not yet run on a
 GPU, checked on the CPU with randomised interleaving models
 (tests/protocol_models.py): the 64-key tree attention's mbarrier protocol
-and the vocab-parallel peer-memory key exchange.  Each model must be clean
+the vocab-parallel peer-memory key exchange, and the exchange fused into
+the shard GEMM.  Each model must be clean
 for the protocol the kernel uses and must catch a known-bad variant (the
 previous final wait of the attention kernel; one parity for the exchange),
 which shows the model can see the bug it guards against."""
@@ -31,5 +32,11 @@ def test_attention_tc2_protocol():
 
 def test_exchange_protocol():
     run = lambda par: (lambda seed: PM.run_exchange(seed, 2 + seed % 7, 6, parities=par))
+    assert _count(run(2), range(300)) == 0
+    assert _count(run(1), range(300)) > 0
+
+
+def test_fused_exchange_protocol():
+    run = lambda par: (lambda seed: PM.run_fused_exchange(seed, 2 + seed % 7, 6, parities=par))
     assert _count(run(2), range(300)) == 0
     assert _count(run(1), range(300)) > 0
