@@ -230,6 +230,8 @@ def vocab_parallel_multi_verify(
     and its last CTA waits for the peers and runs the scan (tensor-core
     dtypes only; same rule on the sequence of calls).
     """
+    if exchange not in ("nccl", "p2p", "fused"):
+        raise ValueError(f"exchange must be 'nccl', 'p2p' or 'fused', got {exchange!r}")
     prim = prim or get_parallel_primitives()
     hidden = hidden.contiguous()
     weight_shard = weight_shard.contiguous()
