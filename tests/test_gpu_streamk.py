@@ -7,8 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.xfail(reason="first GPU run pending", strict=False)]
+pytestmark = [pytest.mark.gpu, pytest.mark.isolated]
 
 INT64_MIN = -(2 ** 63)
 

@@ -13,8 +13,7 @@ import torch
 
 from oracle import mtp_oracle as O
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.xfail(reason="first GPU run pending", strict=False)]
+pytestmark = [pytest.mark.gpu, pytest.mark.isolated]
 
 
 @pytest.fixture(scope="module")

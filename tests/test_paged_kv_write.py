@@ -35,7 +35,7 @@ def mk():
 
 
 @pytest.mark.gpu
-@pytest.mark.xfail(reason="first GPU run pending", strict=False)
+@pytest.mark.isolated
 def test_device_matches_reference(mk, golden):
     g = golden("paged_kv_write.npz")
     d = torch.device("cuda", 0)
@@ -58,7 +58,7 @@ def test_device_matches_reference(mk, golden):
 
 
 @pytest.mark.gpu
-@pytest.mark.xfail(reason="first GPU run pending", strict=False)
+@pytest.mark.isolated
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 def test_device_tree_commit(mk, dt):
     """Commit a path of tree nodes (node_idx) with per-sequence lengths
@@ -90,7 +90,7 @@ def test_device_tree_commit(mk, dt):
 
 
 @pytest.mark.gpu
-@pytest.mark.xfail(reason="first GPU run pending", strict=False)
+@pytest.mark.isolated
 def test_device_bad_page_recorded(mk):
     import _mtp_native as N
     d = torch.device("cuda", 0)

@@ -52,7 +52,7 @@ def mk():
 
 
 @pytest.mark.gpu
-@pytest.mark.xfail(reason="first GPU run pending", strict=False)
+@pytest.mark.isolated
 def test_device_attention(mk, golden):
     g = golden("quant_attention_int4.npz")
     d = torch.device("cuda", 0)
@@ -74,7 +74,7 @@ def test_device_attention(mk, golden):
 
 
 @pytest.mark.gpu
-@pytest.mark.xfail(reason="first GPU run pending", strict=False)
+@pytest.mark.isolated
 def test_device_int4(mk, golden):
     g = golden("quant_attention_int4.npz")
     d = torch.device("cuda", 0)
@@ -87,7 +87,7 @@ def test_device_int4(mk, golden):
 
 
 @pytest.mark.gpu
-@pytest.mark.xfail(reason="first GPU run pending", strict=False)
+@pytest.mark.isolated
 @pytest.mark.parametrize("M,N,K,group,dt", [
     (1, 4096, 4096, 128, torch.bfloat16),   # decode-sized: streamed GEMV kernel, one row of x
     (2, 1000, 1024, 32, torch.float32),
