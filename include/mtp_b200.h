@@ -358,7 +358,10 @@ size_t mtp_verify_exchange_bytes(int64_t rows, int world);
  * hidden/weight_shard: equal 16-bit dtypes with 16-byte rows (tensor
  * cores).  workspace: a verify workspace (mtp_verify_workspace(0) bytes, plus
  * mtp_gemm_streamk_bytes under GEMM schedule 1), put at rest once.  All
- * ranks must make the same sequence of calls with the same B*S. */
+ * ranks must make the same sequence of calls with the same B*S.  After a call
+ * reports MTP_ERR_TIMEOUT (a rank did not arrive), keys may still be landing:
+ * synchronise every rank, then run mtp_verify_fused_init on every buffer
+ * again before the next call. */
 size_t mtp_verify_fused_bytes(int64_t rows, int world);
 int mtp_verify_fused_init(void* buf, int64_t rows, int world, void* stream);
 int mtp_verify_shard_fused(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
