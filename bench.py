@@ -654,6 +654,57 @@ def run_sweep(args):
     ct = cpu_time(lambda: O.fused_multi_verify(hs, lms, None, ds))
     emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16_sus"],
          "measured bf16_tflops_sustained", 2 * S, ct)
+    del lm
+
+    # ---- operators around the path (not BASELINE configs): one line each
+    # tree attention -> RMSNorm -> linear: the reference's own bench geometry
+    # (bench_memory.py:96, fp32) and a draft-head shape (bf16, D = hidden)
+    for (Bm, Hm, Dm, Lm, Nm, dt) in ((64, 4, 64, 32, 256, torch.float32),
+                                    (64, 1, 4096, 64, 32000, torch.bfloat16)):
+        g = torch.Generator(device=dev).manual_seed(5)
+        qm = torch.randn(Bm, Hm, Dm, generator=g, device=dev).to(dt)
+        km = torch.randn(Bm, Hm, Lm, Dm, generator=g, device=dev).to(dt)
+        vm = torch.randn(Bm, Hm, Lm, Dm, generator=g, device=dev).to(dt)
+        mm = (torch.rand(Lm, generator=g, device=dev) > 0.3).float()
+        rw = 1.0 + 0.1 * torch.randn(Dm, generator=g, device=dev)
+        pw = (0.05 * torch.randn(Nm, Dm, generator=g, device=dev)).to(dt)
+        t = time_call(lambda: mk.fused_tree_attn_rmsnorm_linear(qm, km, vm, mm, pw, rms_w=rw), iters)
+        eb = qm.element_size()
+        byts = (2 * Bm * Hm * Lm * Dm + 2 * Bm * Hm * Dm + Nm * Dm) * eb + Bm * Hm * Nm * eb
+        flop = 2.0 * Bm * Hm * Nm * Dm
+        qs, ks, vs, ws_, ms_, rws = f32(qm[:2]), f32(km[:2]), f32(vm[:2]), f32(pw), f32(mm), f32(rw)
+        ct = cpu_time(lambda: O.tree_attn_rmsnorm_linear(qs, ks, vs, ms_, rws, ws_, None, None,
+                                                         1 / math.sqrt(Dm), 1e-6))
+        emit(f"tree_attn_rmsnorm_linear_B{Bm}_H{Hm}_D{Dm}_L{Lm}_N{Nm}", Bm * Hm, "rows/s", t, "hbm",
+             byts / t / 1e9, peaks["hbm"], "measured hbm_gbs", 2 * Hm, ct,
+             {"dtype": "f32" if dt == torch.float32 else "bf16", "tflops": flop / t / 1e12})
+    # INT4 weights, decode-sized M (streamed GEMV)
+    Mi, Ni, Ki, gi = 1, 14336, 4096, 128
+    g = torch.Generator(device=dev).manual_seed(6)
+    pk, sc = mk.quantize_int4(torch.randn(Ni, Ki, generator=g, device=dev), group=gi)
+    xi = torch.randn(Mi, Ki, generator=g, device=dev).to(torch.bfloat16)
+    t = time_call(lambda: mk.fused_int4_matmul(xi, pk, sc, Ki, gi), iters)
+    byts = Ni * Ki / 2 + sc.numel() * 4 + Mi * Ki * 2 + Mi * Ni * 2
+    pks, scs, xis = pk.cpu().numpy(), sc.cpu().numpy(), f32(xi)
+    ct = cpu_time(lambda: O.int4_matmul(xis, pks, scs, Ki, gi))
+    emit("int4_matmul_M1_N14336_K4096_g128", Mi, "rows/s", t, "hbm", byts / t / 1e9, peaks["hbm"],
+         "measured hbm_gbs", Mi, ct, {"dtype": "int4 x bf16"})
+    # FP8 KV-cache decode attention
+    Ba, Ha, La, Da = 16, 32, 4096, 128
+    g = torch.Generator(device=dev).manual_seed(7)
+    qa = torch.randn(Ba, Ha, Da, generator=g, device=dev).to(torch.bfloat16)
+    ka = torch.randn(Ba, Ha, La, Da, generator=g, device=dev).to(torch.float8_e4m3fn)
+    va = torch.randn(Ba, Ha, La, Da, generator=g, device=dev).to(torch.float8_e4m3fn)
+    ksa = torch.rand(Ha, generator=g, device=dev) + 0.5
+    vsa = torch.rand(Ha, generator=g, device=dev) + 0.5
+    t = time_call(lambda: mk.fused_causal_attention_fp8(qa, ka, va, ksa, vsa), iters)
+    byts = 2 * Ba * Ha * La * Da + 2 * 2 * Ba * Ha * Da
+    q0, k0 = f32(qa[:1]), O.e4m3_bits_to_f32(ka[:1].view(torch.uint8).cpu().numpy())
+    v0 = O.e4m3_bits_to_f32(va[:1].view(torch.uint8).cpu().numpy())
+    ks0, vs0 = f32(ksa), f32(vsa)
+    ct = cpu_time(lambda: O.causal_attention_scaled(q0, k0, v0, ks0, vs0, 1 / math.sqrt(Da)))
+    emit("causal_attention_fp8_B16_H32_L4096_D128", Ba * Ha, "query rows/s", t, "hbm", byts / t / 1e9,
+         peaks["hbm"], "measured hbm_gbs", Ha, ct, {"dtype": "e4m3 kv, bf16 q"})
     assert N.device_status(dev) == 0
 
 
