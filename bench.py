@@ -582,6 +582,19 @@ def run_sweep(args):
         print(json.dumps(line), flush=True)
 
     iters = max(5, min(args.steps, 50))
+    # --compare: each GEMM config under both schedules, config 4 under both
+    # attention kernels (one line per variant)
+    gemm_variants = ("dp", "streamk") if args.compare else (args.gemm_schedule,)
+    attn_variants = (1, 2) if args.compare else (N.attn_kernel(),)
+
+    def timed_gemm(fn):
+        out = []
+        for v in gemm_variants:
+            N.set_gemm_schedule(1 if v == "streamk" else 0)
+            out.append((v, time_call(fn, iters)))
+        N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
+        return out
+
     # ---- config 2 sweep: RMSNorm-linear bf16, gamma on
     for M in (64, 512, 2048, 8192):
         K, Nn = C2["K"], C2["N"]
@@ -589,15 +602,17 @@ def run_sweep(args):
         x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
         gam = 1.0 + 0.1 * torch.randn(K, generator=g, device=dev)
         W = (0.02 * torch.randn(Nn, K, generator=g, device=dev)).to(torch.bfloat16)
-        t = time_call(lambda: mk.fused_rmsnorm_linear(x, W, None, C2["eps"], norm_weight=gam), iters)
+        times = timed_gemm(lambda: mk.fused_rmsnorm_linear(x, W, None, C2["eps"], norm_weight=gam))
         flop, byts = 2.0 * M * Nn * K, 2.0 * (M * K + Nn * K + M * Nn)
         tensor = flop / byts > 281  # ridge of the measured peaks
         rows = min(M, 16)
         xs, ws, gs = f32(x[:rows]), f32(W), f32(gam)
         ct = cpu_time(lambda: O.rmsnorm_linear(xs, ws * gs[None, :], None, C2["eps"], 1.0))
-        emit(f"config2_M{M}", M, "rows/s", t, "tensor" if tensor else "hbm",
-             flop / t / 1e12 if tensor else byts / t / 1e9, peaks["bf16_sus"] if tensor else peaks["hbm"],
-             "measured bf16_tflops_sustained" if tensor else "measured hbm_gbs", rows, ct)
+        for v, t in times:
+            emit(f"config2_M{M}", M, "rows/s", t, "tensor" if tensor else "hbm",
+                 flop / t / 1e12 if tensor else byts / t / 1e9, peaks["bf16_sus"] if tensor else peaks["hbm"],
+                 "measured bf16_tflops_sustained" if tensor else "measured hbm_gbs", rows, ct,
+                 {"gemm_schedule": v})
         del x, W
     # ---- config 3: FP8 E4M3, per-token activations, packed per-channel weight scales
     M, K, Nn = 1024, 8192, 28672
@@ -608,16 +623,17 @@ def run_sweep(args):
     wq, sw = mk.quantize_fp8_rows(0.02 * torch.randn(Nn, K, generator=g, device=dev))
     flat, offs = mk.pack_scales([sw])
     swv = mk.unpack_scale_tensor(flat, offs, 0, (Nn,))
-    t = time_call(lambda: mk.fused_rmsnorm_linear_fp8(xq, wq, swv, x_scale=sx, out_dtype=torch.bfloat16), iters)
+    times = timed_gemm(lambda: mk.fused_rmsnorm_linear_fp8(xq, wq, swv, x_scale=sx, out_dtype=torch.bfloat16))
     flop = 2.0 * M * Nn * K
     rows = 4
     xd = O.e4m3_bits_to_f32(xq[:rows].view(torch.uint8).cpu().numpy()) * f32(sx)[:rows, None]
     wd = O.e4m3_bits_to_f32(wq.view(torch.uint8).cpu().numpy())
     sws = f32(sw)
     ct = cpu_time(lambda: O.rmsnorm_linear_fp8(xd, wd, sws, None, 1e-6))
-    emit("config3_fp8", M, "rows/s", t, "tensor", flop / t / 1e12, 2 * peaks["bf16_sus"],
-         "2 x measured bf16_tflops_sustained (nominal fp8:bf16 ratio; fp8 not measured)", rows, ct,
-         {"dtype": "e4m3"})
+    for v, t in times:
+        emit("config3_fp8", M, "rows/s", t, "tensor", flop / t / 1e12, 2 * peaks["bf16_sus"],
+             "2 x measured bf16_tflops_sustained (nominal fp8:bf16 ratio; fp8 not measured)", rows, ct,
+             {"dtype": "e4m3", "gemm_schedule": v})
     del x, xq, wq
     # ---- config 4: paged tree attention
     B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
@@ -634,14 +650,18 @@ def run_sweep(args):
     tk = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
     tv = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
     tmd = torch.tensor(tm, device=dev)
-    t = time_call(lambda: mk.fused_tree_attention_paged(q, kp, vp, tdev, tk, tv, tmd), iters)
+    atimes = []
+    for v in attn_variants:
+        N.set_attn_kernel(v)
+        atimes.append((v, time_call(lambda: mk.fused_tree_attention_paged(q, kp, vp, tdev, tk, tv, tmd), iters)))
     pages0 = table[0].view(-1, ps)[:, 0].long()
     kps, vps = f32(kp[pages0.to(dev)][:, 0:1]), f32(vp[pages0.to(dev)][:, 0:1])
     tab0 = np.repeat(np.arange(pages0.numel(), dtype=np.int32), ps)[None, :]
     q0, tk0, tv0 = f32(q[0:1]), f32(tk[0:1]), f32(tv[0:1])
     ct = cpu_time(lambda: O.tree_attention_paged_fast(q0, kps, vps, tab0, ctx, ps, tk0, tv0, tm, 1 / math.sqrt(D)))
-    emit("config4_tree_attention", B * T, "tree-node queries/s", t, "hbm", C4_BYTES / t / 1e9, peaks["hbm"],
-         "measured hbm_gbs", T, ct, {"tflops": C4_FLOP / t / 1e12})
+    for v, t in atimes:
+        emit("config4_tree_attention", B * T, "tree-node queries/s", t, "hbm", C4_BYTES / t / 1e9, peaks["hbm"],
+             "measured hbm_gbs", T, ct, {"tflops": C4_FLOP / t / 1e12, "attn_kernel": v})
     del kp, vp
     # ---- config 5: fused_multi_verify, tp = 1
     Bv, S, K, V = C5["B"], C5["S"], C5["K"], C5["V"]
@@ -649,11 +669,12 @@ def run_sweep(args):
     hid = torch.randn(Bv, S, K, generator=g, device=dev).to(torch.bfloat16)
     lm = (0.02 * torch.randn(V, K, generator=g, device=dev)).to(torch.bfloat16)
     dr = torch.randint(0, V, (Bv, S - 1), device=dev, dtype=torch.int32)
-    t = time_call(lambda: mv.fused_multi_verify(hid, lm, dr), iters)
+    times = timed_gemm(lambda: mv.fused_multi_verify(hid, lm, dr))
     hs, lms, ds = f32(hid[:2]), f32(lm), dr[:2].cpu().numpy()
     ct = cpu_time(lambda: O.fused_multi_verify(hs, lms, None, ds))
-    emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16_sus"],
-         "measured bf16_tflops_sustained", 2 * S, ct)
+    for v, t in times:
+        emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16_sus"],
+             "measured bf16_tflops_sustained", 2 * S, ct, {"gemm_schedule": v})
     del lm
 
     # ---- operators around the path (not BASELINE configs): one line each
@@ -722,6 +743,8 @@ def main():
     ap.add_argument("--exchange", choices=["nccl", "p2p", "fused"], default="nccl",
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
                          "or the all-reduce fused into the shard GEMM")
+    ap.add_argument("--compare", action="store_true",
+                    help="with --sweep: every GEMM config under both schedules, config 4 under both attention kernels")
     ap.add_argument("--gemm-schedule", choices=["dp", "streamk"], default="dp",
                     help="tensor-core GEMM schedule: whole tiles per CTA, or stream-K where it is faster")
     args = ap.parse_args()

@@ -75,6 +75,14 @@ int mtp_device_status(void* stream, int* code_out, int clear);
 int mtp_set_gemm_schedule(int mode);
 int mtp_gemm_schedule(void);
 
+/* Process-wide choice of the paged tree-attention kernel behind
+ * mtp_tree_attention_paged: 1 (default) = 128-key chunks; 2 = 64-key chunks
+ * with double-buffered scores in tensor memory (shapes it cannot take run
+ * kernel 1).  The environment variable MTP_ATTN_KERNEL=2 sets the initial
+ * value.  Returns MTP_ERR_ARG for other values. */
+int mtp_set_attn_kernel(int version);
+int mtp_attn_kernel(void);
+
 /* Extra workspace bytes that let a GEMM of C[M,N] = A[M,K] B[N,K]^T
  * (ab_dtype: 16-bit or E4M3) run stream-K on the current device; 0 when it
  * would not.  Add it to the operator's own workspace size.  The stream-K

@@ -69,6 +69,8 @@ SIGNATURES = {
     "mtp_verify_exchange_chain": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_set_gemm_schedule": (_i, [_i]),
     "mtp_gemm_schedule": (_i, []),
+    "mtp_set_attn_kernel": (_i, [_i]),
+    "mtp_attn_kernel": (_i, []),
     "mtp_gemm_streamk_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "mtp_gemm_streamk_plan": (_i, [_i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_i64)]),
     "mtp_gemm_streamk_check": (_i, [_i64, _i64, _i64, _i, _i, _i]),
@@ -205,6 +207,15 @@ def set_gemm_schedule(mode: int) -> None:
     with _ws_lock:
         for key in [k for k in _ws if k[2] in _GEMM_WS]:
             del _ws[key]
+
+
+def attn_kernel() -> int:
+    return int(lib().mtp_attn_kernel())
+
+
+def set_attn_kernel(version: int) -> None:
+    """1 = the 128-key tree-attention kernel, 2 = the 64-key kernel."""
+    check(lib().mtp_set_attn_kernel(int(version)), "mtp_set_attn_kernel")
 
 
 def streamk_bytes(M: int, N: int, K: int, ab_code: int) -> int:

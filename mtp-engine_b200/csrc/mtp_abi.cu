@@ -1016,13 +1016,21 @@ int make_map(CUtensorMap* map, const void* base, int dtype, int rank, const uint
   return MTP_OK;
 }
 
-// MTP_ATTN_KERNEL=2 selects tree_attention_tc2_kernel (64-key chunks,
-// double-buffered scores); anything else the 128-key kernel.
+// Tree-attention kernel: 1 = the 128-key kernel (default), 2 =
+// tree_attention_tc2_kernel (64-key chunks, double-buffered scores).  The
+// environment (MTP_ATTN_KERNEL=2) sets the initial choice; mtp_set_attn_kernel
+// changes it.
+std::atomic<int> g_attn_kernel{0};
+
 int attn_kernel_version() {
-  static const int v = [] {
+  int v = g_attn_kernel.load(std::memory_order_relaxed);
+  if (v == 0) {
     const char* e = getenv("MTP_ATTN_KERNEL");
-    return (e && e[0] == '2' && e[1] == 0) ? 2 : 1;
-  }();
+    v = (e && e[0] == '2' && e[1] == 0) ? 2 : 1;
+    int expected = 0;
+    g_attn_kernel.compare_exchange_strong(expected, v);
+    v = g_attn_kernel.load(std::memory_order_relaxed);
+  }
   return v;
 }
 
@@ -1125,6 +1133,14 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
 }  // namespace
 
 extern "C" {
+
+int mtp_set_attn_kernel(int version) {
+  if (version != 1 && version != 2) return fail(MTP_ERR_ARG, "attention kernel %d (expected 1 or 2)", version);
+  g_attn_kernel.store(version, std::memory_order_relaxed);
+  return MTP_OK;
+}
+
+int mtp_attn_kernel(void) { return attn_kernel_version(); }
 
 size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
                                           int64_t ctx_len) {
