@@ -106,7 +106,8 @@ int mtp_gemm_streamk_plan(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms
 
 /* Test support, host only: walks the kernel's work iterator for every CTA of
  * that plan and checks that each (tile, K block) is computed once and that
- * split tiles' parts and slots agree.  MTP_OK or MTP_ERR_SHAPE (message in
+ * split tiles' parts and slots agree.  grid < 0 checks the whole-tile plan
+ * of the same kernel instead.  MTP_OK or MTP_ERR_SHAPE (message in
  * mtp_last_error). */
 int mtp_gemm_streamk_check(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms, int grid);
 

@@ -561,11 +561,12 @@ int mtp_gemm_streamk_plan(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms
 // split tile's parts are numbered 0..parts-1 in K order by consecutive CTAs,
 // and that the slot each part writes is the one the summing part reads.
 int mtp_gemm_streamk_check(int64_t M, int64_t N, int64_t K, int ab_dtype, int sms, int grid) {
-  int64_t info[9];
-  if (int st = mtp_gemm_streamk_plan(M, N, K, ab_dtype, sms, grid, info)) return st;
+  if (M <= 0 || N <= 0 || K <= 0 || sms <= 0 || !valid_dtype(ab_dtype))
+    return fail(MTP_ERR_ARG, "bad stream-K plan arguments");
   const int eb = ab_dtype == MTP_DTYPE_E4M3 ? 1 : 2;
   const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
-  const SkPlan p = sk_plan(M, N, num_kb, sms, grid);
+  // grid < 0: the whole-tile plan the fused vocab-parallel verify falls back to
+  const SkPlan p = grid < 0 ? dp_only_plan(M, N, num_kb, sms) : sk_plan(M, N, num_kb, sms, grid);
   if (p.grid <= 0) return fail(MTP_ERR_SHAPE, "no stream-K schedule for these sizes");
   const sk::Sched& sc = p.s;
   const int64_t T = sc.num_tiles;
