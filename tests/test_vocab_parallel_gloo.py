@@ -74,7 +74,7 @@ def _run(world, case, expect_ranks):
     return out
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_keys_allreduce_matches_full(world):
     g = np.load(GOLDEN)
     full = O.fused_multi_verify(g["h3"], g["w3"], None, g["d3"])
