@@ -24,6 +24,7 @@ CHILDREN = {
     "paged_kv_write": (["test_paged_kv_write.py"], {}, None),
     "quant_attention_int4": (["test_quant_attention_int4.py"], {}, None),
     "verify_step": (["test_verify_step.py"], {}, None),
+    "graphs": (["test_gpu_graphs.py"], {}, None),
     "attention_64key_kernel": (["test_gpu_attention_tc.py", "test_gpu_parity.py"], {"MTP_ATTN_KERNEL": "2"},
                                "attention or edge_cases or device_status"),
 }
