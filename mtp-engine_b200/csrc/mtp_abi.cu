@@ -13,6 +13,8 @@
 #include <stdlib.h>
 #include <stdio.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "mtp_attention.cuh"
 #include "mtp_attention_tc.cuh"
 #include "mtp_attention_tc2.cuh"
@@ -36,6 +38,14 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[MTP_NOALLOC_MAX
 namespace {
 
 constexpr int kAbiVersion = 1;
+
+// A named NVTX range around each compute entry point, so profilers can select
+// an operator by name (ncu --nvtx --nvtx-include); free when no tool is attached.
+struct NvtxScope {
+  explicit NvtxScope(const char* name) { nvtxRangePushA(name); }
+  ~NvtxScope() { nvtxRangePop(); }
+};
+#define MTP_NVTX(name) NvtxScope mtp_nvtx_scope_(name)
 constexpr int kMaxDevices = 64;
 
 thread_local char g_err[512] = "";
@@ -517,6 +527,7 @@ int mtp_attn_trace_read(unsigned long long* host, int n) {
 
 int mtp_gemm_test(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,
                   int force_simt, void* stream) {
+  MTP_NVTX("mtp_gemm_test");
   if (int st = check_dims(M, N, K)) return st;
   if (!valid_dtype(ab_dtype)) return fail(MTP_ERR_DTYPE, "bad dtype");
   if (M == 0 || N == 0) return MTP_OK;
@@ -620,6 +631,7 @@ int mtp_gemm_streamk_check(int64_t M, int64_t N, int64_t K, int ab_dtype, int sm
 
 int mtp_gemm_test_streamk(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,
                           int grid, void* workspace, size_t workspace_bytes, void* stream) {
+  MTP_NVTX("mtp_gemm_test_streamk");
   if (int st = check_dims(M, N, K)) return st;
   if (!valid_dtype(ab_dtype)) return fail(MTP_ERR_DTYPE, "bad dtype");
   if (M == 0 || N == 0) return MTP_OK;
@@ -659,6 +671,7 @@ int mtp_rmsnorm_linear(const void* x, int x_dtype, const void* weight, int w_dty
                        int bias_dtype, const void* norm_weight, int norm_dtype, void* y, int y_dtype, int64_t M,
                        int64_t N, int64_t K, float eps, float scale, void* workspace, size_t workspace_bytes,
                        void* stream) {
+  MTP_NVTX("mtp_rmsnorm_linear");
   if (int st = check_dims(M, N, K)) return st;
   if (!valid_dtype(x_dtype) || !valid_dtype(w_dtype) || !valid_dtype(y_dtype) ||
       x_dtype == MTP_DTYPE_E4M3 || y_dtype == MTP_DTYPE_E4M3)
@@ -697,6 +710,7 @@ int mtp_rmsnorm_linear_fp8(const void* x, int x_dtype, const float* x_scale, con
                            const float* wscale, const void* bias, int bias_dtype, void* y, int y_dtype, int64_t M,
                            int64_t N, int64_t K, float eps, void* workspace, size_t workspace_bytes,
                            void* stream) {
+  MTP_NVTX("mtp_rmsnorm_linear_fp8");
   if (int st = check_dims(M, N, K)) return st;
   if (!valid_dtype(x_dtype) || !valid_dtype(w_dtype) || !valid_dtype(y_dtype) || y_dtype == MTP_DTYPE_E4M3)
     return fail(MTP_ERR_DTYPE, "unsupported dtype combination x=%d w=%d y=%d", x_dtype, w_dtype, y_dtype);
@@ -745,6 +759,7 @@ int mtp_tree_attn_rmsnorm_linear(const void* q, const void* k, const void* v, in
                                  int bias_dtype, const float* wscale, void* out, int64_t B, int64_t H, int64_t L,
                                  int64_t D, int64_t N, float scale, float eps, void* workspace,
                                  size_t workspace_bytes, void* stream) {
+  MTP_NVTX("mtp_tree_attn_rmsnorm_linear");
   if (B < 0 || H < 0 || L < 0 || D <= 0 || N < 0) return fail(MTP_ERR_SHAPE, "bad sizes");
   if (D > rowattn::kMaxD) return fail(MTP_ERR_SHAPE, "D=%lld above %d", (long long)D, rowattn::kMaxD);
   if (!valid_dtype(qkv_dtype) || qkv_dtype == MTP_DTYPE_E4M3 || !valid_dtype(w_dtype))
@@ -783,6 +798,7 @@ int mtp_paged_kv_write(void* k_pages, void* v_pages, int dtype, const int32_t* p
                        int64_t num_pages, int64_t page_size, const void* src_k, const void* src_v, int src_dtype,
                        int64_t src_len, const int32_t* node_idx, const int32_t* count, int64_t B, int64_t H,
                        int64_t D, int64_t start, int64_t n, void* stream) {
+  MTP_NVTX("mtp_paged_kv_write");
   if (B < 0 || H < 0 || D <= 0 || n < 0 || src_len < 0 || page_size <= 0 || num_pages < 0 || start < 0)
     return fail(MTP_ERR_SHAPE, "bad KV write sizes");
   if (start + n > table_stride) return fail(MTP_ERR_SHAPE, "logical positions [%lld, %lld) beyond the page table",
@@ -835,6 +851,7 @@ static int launch_decode_attention(const AttnArgs& a, cudaStream_t s) {
 
 int mtp_tree_attention(const void* q, const void* k, const void* v, const float* mask, void* out, int dtype,
                        int64_t B, int64_t H, int64_t L, int64_t D, float scale, void* stream) {
+  MTP_NVTX("mtp_tree_attention");
   if (B < 0 || H < 0 || L < 0 || D <= 0) return fail(MTP_ERR_SHAPE, "bad attention sizes");
   if (!valid_dtype(dtype) || dtype == MTP_DTYPE_E4M3) return fail(MTP_ERR_DTYPE, "unsupported dtype %d", dtype);
   if (B * H == 0) return MTP_OK;
@@ -860,6 +877,7 @@ int mtp_tree_attention(const void* q, const void* k, const void* v, const float*
 int mtp_causal_attention_scaled(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype,
                                 const float* kscale, const float* vscale, void* out, int64_t B, int64_t H, int64_t L,
                                 int64_t D, float scale, void* stream) {
+  MTP_NVTX("mtp_causal_attention_scaled");
   if (B < 0 || H < 0 || L < 0 || D <= 0) return fail(MTP_ERR_SHAPE, "bad attention sizes");
   if (!valid_dtype(q_dtype) || q_dtype == MTP_DTYPE_E4M3 || !valid_dtype(kv_dtype))
     return fail(MTP_ERR_DTYPE, "unsupported dtypes q=%d kv=%d", q_dtype, kv_dtype);
@@ -889,6 +907,7 @@ int mtp_causal_attention_scaled(const void* q, int q_dtype, const void* k, const
 
 int mtp_int4_matmul(const void* x, int x_dtype, const uint8_t* packed, const float* scales, int64_t group, void* y,
                     int y_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
+  MTP_NVTX("mtp_int4_matmul");
   if (int st = check_dims(M, N, K)) return st;
   if (K % 2 != 0) return fail(MTP_ERR_SHAPE, "K=%lld must be even (two codes per byte)", (long long)K);
   if (group <= 0) return fail(MTP_ERR_SHAPE, "group must be positive");
@@ -920,6 +939,7 @@ int mtp_int4_matmul(const void* x, int x_dtype, const uint8_t* packed, const flo
 int mtp_paged_attention(const void* q, const void* k_pages, const void* v_pages, const int32_t* page_table,
                         void* out, int dtype, int64_t B, int64_t H, int64_t L, int64_t D, int64_t num_pages,
                         int64_t page_size, float scale, void* stream) {
+  MTP_NVTX("mtp_paged_attention");
   if (B < 0 || H < 0 || L < 0 || D <= 0 || page_size <= 0 || num_pages < 0)
     return fail(MTP_ERR_SHAPE, "bad paged attention sizes");
   if (!valid_dtype(dtype) || dtype == MTP_DTYPE_E4M3) return fail(MTP_ERR_DTYPE, "unsupported dtype %d", dtype);
@@ -1157,6 +1177,7 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
                              const float* tree_mask, void* out, int dtype, int64_t B, int64_t T, int64_t Hq,
                              int64_t Hkv, int64_t D, int64_t num_pages, int64_t page_size, float scale,
                              void* workspace, size_t workspace_bytes, void* stream) {
+  MTP_NVTX("mtp_tree_attention_paged");
   if (B < 0 || T < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || ctx_len < 0 || page_size <= 0 || num_pages < 0)
     return fail(MTP_ERR_SHAPE, "bad tree attention sizes");
   if (Hq % Hkv != 0) return fail(MTP_ERR_SHAPE, "Hq=%lld not a multiple of Hkv=%lld", (long long)Hq, (long long)Hkv);
@@ -1254,6 +1275,7 @@ static int verify_common(const void* hidden, int h_dtype, const void* weight, in
 int mtp_fused_verify(const void* hidden, int h_dtype, const void* weight, int w_dtype, const void* bias,
                      int bias_dtype, const int32_t* draft, int8_t* accept, int32_t* top, int64_t M, int64_t K,
                      int64_t V, void* workspace, size_t workspace_bytes, void* stream) {
+  MTP_NVTX("mtp_fused_verify");
   if (M == 0) return MTP_OK;
   if (!draft || !accept || !top) return fail(MTP_ERR_ARG, "null output pointer");
   GemmEpilogue ep{};
@@ -1271,6 +1293,7 @@ int mtp_fused_multi_verify(const void* hidden, int h_dtype, const void* weight, 
                            int bias_dtype, const int32_t* draft, int8_t* accept, int32_t* accepted_n,
                            int32_t* corrected, int64_t B, int64_t S, int64_t K, int64_t V, void* workspace,
                            size_t workspace_bytes, void* stream) {
+  MTP_NVTX("mtp_fused_multi_verify");
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1 (S == D + 1), got S=%lld", (long long)S);
   if (B == 0) return MTP_OK;
   if ((S > 1 && (!draft || !accept)) || !accepted_n || !corrected) return fail(MTP_ERR_ARG, "null output pointer");
@@ -1292,6 +1315,7 @@ int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* 
                                    const void* bias, int bias_dtype, const int32_t* draft, int8_t* accept,
                                    int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S, int64_t K,
                                    int64_t V, void* stream) {
+  MTP_NVTX("mtp_fused_multi_verify_noalloc");
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1 (S == D + 1), got S=%lld", (long long)S);
   if (B == 0) return MTP_OK;
   const int64_t rows = B * S;
@@ -1332,6 +1356,7 @@ int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* 
 int mtp_verify_shard_keys(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
                           const void* bias_shard, int bias_dtype, int64_t* keys, int64_t M, int64_t K,
                           int64_t V_shard, int64_t vocab_offset, void* stream) {
+  MTP_NVTX("mtp_verify_shard_keys");
   if (int st = check_dims(M, V_shard, K)) return st;
   if (M == 0 || V_shard == 0) return MTP_OK;
   if (vocab_offset < 0 || vocab_offset + V_shard > 0xFFFFFFFFLL) return fail(MTP_ERR_SHAPE, "vocab offset out of range");
@@ -1352,6 +1377,7 @@ int mtp_verify_shard_keys_ws(const void* hidden, int h_dtype, const void* weight
                              const void* bias_shard, int bias_dtype, int64_t* keys, int64_t M, int64_t K,
                              int64_t V_shard, int64_t vocab_offset, void* workspace, size_t workspace_bytes,
                              void* stream) {
+  MTP_NVTX("mtp_verify_shard_keys_ws");
   if (int st = check_dims(M, V_shard, K)) return st;
   if (M == 0 || V_shard == 0) return MTP_OK;
   if (vocab_offset < 0 || vocab_offset + V_shard > 0xFFFFFFFFLL) return fail(MTP_ERR_SHAPE, "vocab offset out of range");
@@ -1371,6 +1397,7 @@ int mtp_verify_shard_keys_ws(const void* hidden, int h_dtype, const void* weight
 
 int mtp_verify_step(const int32_t* draft, const int32_t* accepted_n, const int32_t* corrected, int64_t B, int64_t D,
                     int32_t* step_tokens, int64_t ld, int32_t* info, void* stream) {
+  MTP_NVTX("mtp_verify_step");
   if (B < 0 || D < 0 || ld < D || D > INT32_MAX) return fail(MTP_ERR_SHAPE, "bad step sizes");
   if (!accepted_n || !info || (B > 0 && !corrected) || (B > 0 && D > 0 && (!draft || !step_tokens)))
     return fail(MTP_ERR_ARG, "null pointer");
@@ -1403,6 +1430,7 @@ int mtp_verify_shard_fused(const void* hidden, int h_dtype, const void* weight_s
                            const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected, int64_t B,
                            int64_t S, int64_t K, int64_t V_shard, int64_t vocab_offset, void* workspace,
                            size_t workspace_bytes, void* stream) {
+  MTP_NVTX("mtp_verify_shard_fused");
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1");
   if (world < 1 || rank < 0 || rank >= world) return fail(MTP_ERR_ARG, "rank %d / world %d", rank, world);
   const int64_t rows = B * S;
@@ -1456,6 +1484,7 @@ size_t mtp_verify_exchange_bytes(int64_t rows, int world) {
 int mtp_verify_exchange_chain(int64_t* keys, const void* peer_bufs, int rank, int world, uint64_t* epoch,
                               const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected,
                               int64_t B, int64_t S, void* stream) {
+  MTP_NVTX("mtp_verify_exchange_chain");
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1");
   if (world < 1 || rank < 0 || rank >= world) return fail(MTP_ERR_ARG, "rank %d / world %d", rank, world);
   if (B == 0) return MTP_OK;
@@ -1479,6 +1508,7 @@ int mtp_verify_exchange_chain(int64_t* keys, const void* peer_bufs, int rank, in
 
 int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* accept, int32_t* accepted_n,
                                int32_t* corrected, int64_t B, int64_t S, void* stream) {
+  MTP_NVTX("mtp_verify_chain_from_keys");
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1");
   if (B == 0) return MTP_OK;
   if (!keys || (S > 1 && (!draft || !accept)) || !accepted_n || !corrected) return fail(MTP_ERR_ARG, "null pointer");
