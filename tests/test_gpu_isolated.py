@@ -25,6 +25,7 @@ CHILDREN = {
     "quant_attention_int4": (["test_quant_attention_int4.py"], {}, None),
     "verify_step": (["test_verify_step.py"], {}, None),
     "graphs": (["test_gpu_graphs.py"], {}, None),
+    "canary": (["test_gpu_canary.py"], {}, None),
     "attention_64key_kernel": (["test_gpu_attention_tc.py", "test_gpu_parity.py"], {"MTP_ATTN_KERNEL": "2"},
                                "attention or edge_cases or device_status"),
 }
