@@ -124,7 +124,8 @@ def dtype_code(t: torch.Tensor) -> int:
 
 
 def ptr(t: Optional[torch.Tensor]):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """Device address of t (None for NULL); the bound argtypes take plain ints."""
+    return None if t is None else t.data_ptr()
 
 
 def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
@@ -144,8 +145,16 @@ def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
     return dev
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device):
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    """The current torch stream of `device` as a cudaStream_t value (without
+    building a torch Stream object on every call)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 # --------------------------------------------------------------------------- #
