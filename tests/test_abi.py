@@ -89,3 +89,48 @@ def test_attn_kernel_switch_roundtrip():
         assert N.lib().mtp_set_attn_kernel(3) == 8  # MTP_ERR_ARG
     finally:
         N.set_attn_kernel(before)
+
+
+def test_new_entry_points_checks_without_launch():
+    """Empty sizes return MTP_OK and bad arguments their status, all on the
+    host before any CUDA call (this machine has no GPU: a CUDA call would
+    surface as MTP_ERR_CUDA) and without launching anything."""
+    import _mtp_native as N
+    L = N.lib()
+    p = ctypes.c_void_p(256)  # never dereferenced: every call below returns before a launch
+    before = L.mtp_launch_count()
+    OK, SHAPE, DTYPE, ARG = 0, 1, 2, 8
+    # tree attention -> RMSNorm -> linear
+    assert L.mtp_tree_attn_rmsnorm_linear(p, p, p, 1, None, None, p, 1, None, 0, None, p, 0, 4, 8, 64, 16, 0.1,
+                                          1e-6, None, 0, None) == OK
+    assert L.mtp_tree_attn_rmsnorm_linear(p, p, p, 1, None, None, p, 1, None, 0, None, p, 2, 4, 8, 9000, 16,
+                                          0.1, 1e-6, None, 0, None) == SHAPE  # D above 8192
+    assert L.mtp_tree_attn_rmsnorm_linear(p, p, p, 3, None, None, p, 1, None, 0, None, p, 2, 4, 8, 64, 16, 0.1,
+                                          1e-6, None, 0, None) == DTYPE  # E4M3 queries
+    assert L.mtp_tree_attn_rmsnorm_linear(None, p, p, 1, None, None, p, 1, None, 0, None, p, 2, 4, 8, 64, 16,
+                                          0.1, 1e-6, None, 0, None) == ARG
+    # paged KV write
+    assert L.mtp_paged_kv_write(p, p, 1, p, 64, 8, 16, p, p, 1, 4, None, None, 2, 2, 64, 0, 0, None) == OK
+    assert L.mtp_paged_kv_write(p, p, 1, p, 64, 8, 16, p, p, 1, 4, None, None, 2, 2, 64, 62, 4, None) == SHAPE
+    assert L.mtp_paged_kv_write(p, p, 1, p, 64, 8, 16, p, p, 1, 4, None, None, 2, 2, 64, 0, 5, None) == SHAPE
+    assert L.mtp_paged_kv_write(p, p, 3, p, 64, 8, 16, p, p, 1, 4, None, None, 2, 2, 64, 0, 4, None) == DTYPE
+    assert L.mtp_paged_kv_write(None, p, 1, p, 64, 8, 16, p, p, 1, 4, None, None, 2, 2, 64, 0, 4, None) == ARG
+    # verify step
+    assert L.mtp_verify_step(p, p, p, 0, 4, p, 5, p, None) == OK
+    assert L.mtp_verify_step(p, p, p, 2, 4, p, 3, p, None) == SHAPE  # ld < D
+    assert L.mtp_verify_step(p, None, p, 2, 4, p, 5, p, None) == ARG
+    # FP8-KV attention and INT4 matmul
+    assert L.mtp_causal_attention_scaled(p, 1, p, p, 3, None, None, p, 0, 4, 8, 64, 0.1, None) == OK
+    assert L.mtp_causal_attention_scaled(p, 3, p, p, 3, None, None, p, 2, 4, 8, 64, 0.1, None) == DTYPE
+    assert L.mtp_int4_matmul(p, 1, p, p, 32, p, 1, 0, 16, 64, None) == OK
+    assert L.mtp_int4_matmul(p, 1, p, p, 32, p, 1, 2, 16, 63, None) == SHAPE  # K odd
+    assert L.mtp_int4_matmul(p, 1, p, p, 0, p, 1, 2, 16, 64, None) == SHAPE  # group 0
+    assert L.mtp_int4_matmul(p, 1, None, p, 32, p, 1, 2, 16, 64, None) == ARG
+    # fused vocab-parallel verify and the exchange
+    assert L.mtp_verify_shard_fused(p, 1, p, 1, None, 0, p, 0, 2, p, p, p, p, 0, 6, 64, 128, 0, p, 256,
+                                    None) == OK
+    assert L.mtp_verify_shard_fused(p, 1, p, 1, None, 0, p, 2, 2, p, p, p, p, 4, 6, 64, 128, 0, p, 256,
+                                    None) == ARG  # rank out of range
+    assert L.mtp_verify_fused_bytes(384, 8) >= 2 * 384 * 8 + 2 * 8 * 8 + 8
+    assert L.mtp_verify_exchange_bytes(384, 8) == 2 * 8 * 384 * 8 + 2 * 8 * 8
+    assert L.mtp_launch_count() == before
