@@ -302,11 +302,11 @@ class VocabParallelVerify:
 
     @classmethod
     def from_full(cls, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
-                  prim: Optional[ParallelPrimitives] = None) -> "VocabParallelVerify":
+                  prim: Optional[ParallelPrimitives] = None, exchange: str = "nccl") -> "VocabParallelVerify":
         prim = prim or get_parallel_primitives()
         w, off = shard_lm_head(weight, prim.tp_size, prim.rank)
         b = None if bias is None else bias[off:off + w.shape[0]]
-        return cls(w, off, b, prim)
+        return cls(w, off, b, prim, exchange)
 
     def __call__(self, hidden: torch.Tensor, draft: torch.Tensor,
                  bias_shard: Optional[torch.Tensor] = None):
