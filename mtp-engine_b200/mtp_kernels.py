@@ -14,12 +14,20 @@ Operators provided here (reference file:line):
   fused_tree_attention       mtp_kernels.py:1165-1191
   fused_paged_attention      mtp_kernels.py:1136-1162
   fused_tree_attention_paged (new: paged context + tree nodes, GQA)
-  quantize_fp8_e4m3 / dequantize_fp8 / pack_scales / unpack_scale_tensor
-                             mtp_kernels.py:704-727, 1336-1353
+  fused_tree_attn_rmsnorm_linear
+                             mtp_kernels.py:1222-1250
+  fused_causal_attention     mtp_kernels.py:980-1006
+  fused_causal_attention_fp8 mtp_kernels.py:1105-1133
+  fused_int4_matmul          mtp_kernels.py:1194-1219
+  paged_kv_write             (new: batched PagedKVCache.write_inplace, mtp_engine.py:582-586)
+  quantize_fp8_e4m3 / dequantize_fp8 / quantize_int4 / dequantize_int4 /
+  pack_scales / unpack_scale_tensor
+                             mtp_kernels.py:704-767, 1336-1353
   TUNING / KernelTuningConfig / MAX_FP8 / build_tuning_config (API compatibility)
 
-Operators of the reference module that are not on the verification hot path
-(causal / int4 / bitmask attention, add-rmsnorm, ...) are not reimplemented.
+Operators of the reference module that are not on the verification path
+(bitmask attention, add-rmsnorm, autotuning wrappers, ...) are not
+reimplemented.
 If MTP_REFERENCE_PATH names a checkout of the reference, such names resolve
 to the reference's own implementation (so ``from mtp_kernels import ...`` in
 the reference's engine keeps working); otherwise they raise AttributeError.
