@@ -8,6 +8,10 @@ is ever written -- and whose last CTA decodes the keys into the acceptance
 outputs.  bf16/f16 hidden + weight run on the tensor cores with fp32
 accumulation; fp32 inputs run an IEEE fp32 CUDA-core GEMM, matching the
 reference's fp32 logits (mtp_fused_verify.py:179-181).
+
+Also ``verify_step`` / ``fused_multi_verify_step``: the host step the
+reference's generate loops run after the verify (batch-min rollback index
+and the step's tokens, mtp_engine.py:1244-1258, 1326-1337), on the device.
 """
 
 from __future__ import annotations
