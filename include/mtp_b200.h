@@ -400,6 +400,12 @@ int mtp_keys_fill(int64_t* keys, int64_t n, void* stream);
  * devices).  Benchmarks read it around a timed region. */
 uint64_t mtp_launch_count(void);
 
+/* Test support, host memory only: the argmax key packing the kernels use
+ * (key = order-preserving int32 of the fp32 value << 32 | 0xFFFFFFFF - index;
+ * max over keys = largest value, lowest index among equals) and its decode. */
+int mtp_keys_pack_host(const float* values, const uint32_t* index, int64_t* keys, int64_t n);
+int mtp_keys_index_host(const int64_t* keys, int32_t* index, int64_t n);
+
 /* Test support (no counterpart in the reference): C[M,N] (fp32) = A[M,K] @ B[N,K]^T
  * through the GEMM mainloop the operators use -- the tcgen05 kernel when
  * force_simt == 0 and the operands qualify (bf16/f16/E4M3, 16-byte rows),

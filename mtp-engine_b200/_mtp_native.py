@@ -75,6 +75,8 @@ SIGNATURES = {
     "mtp_gemm_streamk_plan": (_i, [_i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_i64)]),
     "mtp_gemm_streamk_check": (_i, [_i64, _i64, _i64, _i, _i, _i]),
     "mtp_gemm_test_streamk": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _i, _vp, _sz, _vp]),
+    "mtp_keys_pack_host": (_i, [_vp, _vp, _vp, _i64]),
+    "mtp_keys_index_host": (_i, [_vp, _vp, _i64]),
     "mtp_launch_count": (ctypes.c_uint64, []),
     "mtp_gemm_test": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _i, _vp]),
     "mtp_fused_multi_verify_noalloc": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64,

@@ -650,6 +650,20 @@ int mtp_gemm_test_streamk(const void* A, const void* B, int ab_dtype, float* C, 
                         workspace_bytes, g);
 }
 
+// Test support, host memory only: the device code's own key packing
+// (ordered_i32 / make_key / key_index are __host__ __device__).
+int mtp_keys_pack_host(const float* values, const uint32_t* index, int64_t* keys, int64_t n) {
+  if (n < 0 || (n > 0 && (!values || !index || !keys))) return fail(MTP_ERR_ARG, "bad key arguments");
+  for (int64_t i = 0; i < n; ++i) keys[i] = make_key(ordered_i32(values[i]), index[i]);
+  return MTP_OK;
+}
+
+int mtp_keys_index_host(const int64_t* keys, int32_t* index, int64_t n) {
+  if (n < 0 || (n > 0 && (!keys || !index))) return fail(MTP_ERR_ARG, "bad key arguments");
+  for (int64_t i = 0; i < n; ++i) index[i] = key_index(keys[i]);
+  return MTP_OK;
+}
+
 int mtp_device_status(void* stream, int* code_out, int clear) {
   MTP_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
   int code = 0;

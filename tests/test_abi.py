@@ -134,3 +134,32 @@ def test_new_entry_points_checks_without_launch():
     assert L.mtp_verify_fused_bytes(384, 8) >= 2 * 384 * 8 + 2 * 8 * 8 + 8
     assert L.mtp_verify_exchange_bytes(384, 8) == 2 * 8 * 384 * 8 + 2 * 8 * 8
     assert L.mtp_launch_count() == before
+
+
+def test_key_packing_matches_oracle():
+    """The kernels' own key packing (run on the host) equals the oracle's,
+    bit for bit, and max over keys is torch.argmax's rule."""
+    import numpy as np
+    import _mtp_native as N
+    from oracle import mtp_oracle as O
+    special = np.array([0.0, -0.0, 1.0, -1.0, np.inf, -np.inf, 1e-45, -1e-45, 1.17e-38, -1.17e-38,
+                        3.4028235e38, -3.4028235e38, 0.5, 0.5, 2.0, -2.0], dtype=np.float32)
+    rng = np.random.default_rng(0)
+    vals = np.concatenate([special, rng.standard_normal(5000).astype(np.float32) * 100,
+                           rng.integers(-3, 4, 2000).astype(np.float32)])
+    idx = rng.integers(0, 2 ** 31, vals.size).astype(np.uint32)
+    idx[:16] = np.arange(16, dtype=np.uint32)
+    keys = np.empty(vals.size, np.int64)
+    assert N.lib().mtp_keys_pack_host(vals.ctypes.data, idx.ctypes.data, keys.ctypes.data, vals.size) == 0
+    assert np.array_equal(keys, O.pack_key(vals, idx))
+    back = np.empty(vals.size, np.int32)
+    assert N.lib().mtp_keys_index_host(keys.ctypes.data, back.ctypes.data, vals.size) == 0
+    assert np.array_equal(back, idx.astype(np.int32))
+    # argmax rule on a row with ties: the first (lowest-index) maximum wins
+    row = rng.integers(-3, 4, 1000).astype(np.float32)
+    k = O.pack_key(row, np.arange(row.size, dtype=np.uint32))
+    assert int(O.key_index(k.max())) == int(np.argmax(row))
+    # value order: keys order like the values (distinct values)
+    v = np.unique(rng.standard_normal(300).astype(np.float32))
+    kk = O.pack_key(v, np.zeros(v.size, np.uint32))
+    assert np.all(np.diff(kk) > 0)
