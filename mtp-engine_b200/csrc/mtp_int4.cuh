@@ -87,19 +87,21 @@ __global__ void __launch_bounds__(256)
 // 8 warps per block, gemv_rows_per_warp(MR) weight rows per warp (fewer as
 // MR grows, to keep the rows x MR accumulators in registers); each lane owns
 // 32 consecutive K codes (one 16-byte load per row and 1024-element chunk).  x is staged
-// per chunk in shared memory transposed within 32-element groups, so lane l
-// reading code j of its vector hits bank l.  Per-lane partial sums, then a
+// per chunk in shared memory transposed within 32-element groups, padded to 33
+// words per group, so both the staging stores (consecutive K) and the reads
+// (lane l, code j) fall in distinct banks.  Per-lane partial sums, then a
 // warp reduction.  Needs K % 32 == 0 and a 16-byte-aligned packed array.
 __host__ __device__ constexpr int gemv_rows_per_warp(int mr) { return mr <= 2 ? 8 : (mr == 4 ? 4 : 2); }
 __host__ __device__ constexpr int gemv_block_rows(int mr) { return 8 * gemv_rows_per_warp(mr); }
 constexpr int kGemvKC = 1024;
+constexpr int kGemvPitch = 33;  // words per 32-code group in the staged x
 
 template <int MR>
 __global__ void __launch_bounds__(256)
     int4_gemv_kernel(const void* x, int x_dt, const uint8_t* __restrict__ packed, const float* __restrict__ scales,
                      int group, void* y, int y_dt, int M, int N, int K) {
   constexpr int kGemvRowsPerWarp = gemv_rows_per_warp(MR);
-  __shared__ float xs[MR][kGemvKC];
+  __shared__ float xs[MR][32 * kGemvPitch];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * gemv_block_rows(MR) + warp * kGemvRowsPerWarp;
   const int64_t row_bytes = K / 2;
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
     for (int i = threadIdx.x; i < MR * kGemvKC; i += 256) {
       const int m = i / kGemvKC, kl = i % kGemvKC, k = kc + kl;
-      xs[m][(kl & 31) * 32 + (kl >> 5)] = (m < M && k < K) ? load_f32(x, x_dt, (int64_t)m * K + k) : 0.f;
+      xs[m][(kl & 31) * kGemvPitch + (kl >> 5)] = (m < M && k < K) ? load_f32(x, x_dt, (int64_t)m * K + k) : 0.f;
     }
     __syncthreads();
     const int kb = kc + lane * 32;  // this lane's codes kb .. kb + 31
@@ -141,7 +143,7 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < 32; ++j) {
       float xv[MR];
 #pragma unroll
-      for (int m = 0; m < MR; ++m) xv[m] = xs[m][j * 32 + lane];
+      for (int m = 0; m < MR; ++m) xv[m] = xs[m][j * kGemvPitch + lane];
 #pragma unroll
       for (int r = 0; r < kGemvRowsPerWarp; ++r) {
         const int code = (int)((wd[r][j >> 3] >> (4 * (j & 7))) & 0xFu);
