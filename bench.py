@@ -699,6 +699,36 @@ def run_sweep(args):
         emit(f"tree_attn_rmsnorm_linear_B{Bm}_H{Hm}_D{Dm}_L{Lm}_N{Nm}", Bm * Hm, "rows/s", t, "hbm",
              byts / t / 1e9, peaks["hbm"], "measured hbm_gbs", 2 * Hm, ct,
              {"dtype": "f32" if dt == torch.float32 else "bf16", "tflops": flop / t / 1e12})
+    # the reference's single-query operators (CUDA-core decode kernel): paged
+    # attention over a config-4-sized context, tree attention over 512 keys
+    Bd, Hd, Ld, Dd, psd = 16, 32, 4096, 128, 16
+    g = torch.Generator(device=dev).manual_seed(8)
+    Pd = Bd * Ld // psd // Bd + 1
+    kpd = torch.randn(Pd, Bd, Hd, psd, Dd, generator=g, device=dev).to(torch.bfloat16)
+    vpd = torch.randn(Pd, Bd, Hd, psd, Dd, generator=g, device=dev).to(torch.bfloat16)
+    tab = torch.stack([torch.randperm(Pd - 1, generator=torch.Generator().manual_seed(b))[: Ld // psd]
+                       .repeat_interleave(psd) for b in range(Bd)]).to(torch.int32)
+    qd = torch.randn(Bd, Hd, Dd, generator=g, device=dev).to(torch.bfloat16)
+    tabd = tab.to(dev)
+    t = time_call(lambda: mk.fused_paged_attention(qd, kpd, vpd, tabd, psd), iters)
+    byts = 2 * Bd * Hd * Ld * Dd * 2 + 2 * Bd * Hd * Dd * 2
+    kps_, vps_ = f32(kpd[:, 0:1]), f32(vpd[:, 0:1])
+    q1, tab1 = f32(qd[0:1]), tab[0:1].numpy()
+    ct = cpu_time(lambda: O.paged_attention(q1, kps_, vps_, tab1, psd, 1 / math.sqrt(Dd)))
+    emit("paged_attention_B16_H32_L4096_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9, peaks["hbm"],
+         "measured hbm_gbs", Hd, ct)
+    del kpd, vpd
+    Lt = 512
+    kt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
+    vt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
+    mt = (torch.rand(Lt, generator=g, device=dev) > 0.2).float()
+    t = time_call(lambda: mk.fused_tree_attention(qd, kt, vt, mt), iters)
+    byts = 2 * Bd * Hd * Lt * Dd * 2 + 2 * Bd * Hd * Dd * 2
+    kt1, vt1, mt1 = f32(kt[0:1]), f32(vt[0:1]), f32(mt)
+    ct = cpu_time(lambda: O.tree_attention(q1, kt1, vt1, mt1, 1 / math.sqrt(Dd)))
+    emit("tree_attention_B16_H32_L512_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9, peaks["hbm"],
+         "measured hbm_gbs", Hd, ct)
+    del kt, vt
     # INT4 weights, decode-sized M (streamed GEMV)
     Mi, Ni, Ki, gi = 1, 14336, 4096, 128
     g = torch.Generator(device=dev).manual_seed(6)
