@@ -710,24 +710,35 @@ def run_sweep(args):
                        .repeat_interleave(psd) for b in range(Bd)]).to(torch.int32)
     qd = torch.randn(Bd, Hd, Dd, generator=g, device=dev).to(torch.bfloat16)
     tabd = tab.to(dev)
-    t = time_call(lambda: mk.fused_paged_attention(qd, kpd, vpd, tabd, psd), iters)
+    decode_variants = (1, 2) if args.compare else (N.decode_kernel(),)
+
+    def timed_decode(fn):
+        out = []
+        for v in decode_variants:
+            N.set_decode_kernel(v)
+            out.append((v, time_call(fn, iters)))
+        return out
+
+    times = timed_decode(lambda: mk.fused_paged_attention(qd, kpd, vpd, tabd, psd))
     byts = 2 * Bd * Hd * Ld * Dd * 2 + 2 * Bd * Hd * Dd * 2
     kps_, vps_ = f32(kpd[:, 0:1]), f32(vpd[:, 0:1])
     q1, tab1 = f32(qd[0:1]), tab[0:1].numpy()
     ct = cpu_time(lambda: O.paged_attention(q1, kps_, vps_, tab1, psd, 1 / math.sqrt(Dd)))
-    emit("paged_attention_B16_H32_L4096_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9, peaks["hbm"],
-         "measured hbm_gbs", Hd, ct)
+    for v, t in times:
+        emit("paged_attention_B16_H32_L4096_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9,
+             peaks["hbm"], "measured hbm_gbs", Hd, ct, {"decode_kernel": v})
     del kpd, vpd
     Lt = 512
     kt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
     vt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
     mt = (torch.rand(Lt, generator=g, device=dev) > 0.2).float()
-    t = time_call(lambda: mk.fused_tree_attention(qd, kt, vt, mt), iters)
+    times = timed_decode(lambda: mk.fused_tree_attention(qd, kt, vt, mt))
     byts = 2 * Bd * Hd * Lt * Dd * 2 + 2 * Bd * Hd * Dd * 2
     kt1, vt1, mt1 = f32(kt[0:1]), f32(vt[0:1]), f32(mt)
     ct = cpu_time(lambda: O.tree_attention(q1, kt1, vt1, mt1, 1 / math.sqrt(Dd)))
-    emit("tree_attention_B16_H32_L512_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9, peaks["hbm"],
-         "measured hbm_gbs", Hd, ct)
+    for v, t in times:
+        emit("tree_attention_B16_H32_L512_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9,
+             peaks["hbm"], "measured hbm_gbs", Hd, ct, {"decode_kernel": v})
     del kt, vt
     # INT4 weights, decode-sized M (streamed GEMV)
     Mi, Ni, Ki, gi = 1, 14336, 4096, 128
@@ -774,7 +785,8 @@ def main():
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
                          "or the all-reduce fused into the shard GEMM")
     ap.add_argument("--compare", action="store_true",
-                    help="with --sweep: every GEMM config under both schedules, config 4 under both attention kernels")
+                    help="with --sweep: every GEMM config under both schedules, config 4 under both attention "
+                         "kernels, the single-query lines under both decode kernels")
     ap.add_argument("--gemm-schedule", choices=["dp", "streamk"], default="dp",
                     help="tensor-core GEMM schedule: whole tiles per CTA, or stream-K where it is faster")
     args = ap.parse_args()

@@ -83,6 +83,15 @@ int mtp_gemm_schedule(void);
 int mtp_set_attn_kernel(int version);
 int mtp_attn_kernel(void);
 
+/* Process-wide choice of the single-query kernel behind mtp_tree_attention
+ * and mtp_paged_attention: 1 (default) = one warp per key with scalar loads;
+ * 2 = 16-byte loads with several keys in flight per lane and P V split over
+ * key groups, for 16-bit K/V with a power-of-two head size up to 256 (other
+ * shapes run kernel 1).  MTP_DECODE_KERNEL=2 sets the initial value.
+ * Returns MTP_ERR_ARG for other values. */
+int mtp_set_decode_kernel(int version);
+int mtp_decode_kernel(void);
+
 /* Extra workspace bytes that let a GEMM of C[M,N] = A[M,K] B[N,K]^T
  * (ab_dtype: 16-bit or E4M3) run stream-K on the current device; 0 when it
  * would not.  Add it to the operator's own workspace size.  The stream-K

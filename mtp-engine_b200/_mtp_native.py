@@ -71,6 +71,8 @@ SIGNATURES = {
     "mtp_gemm_schedule": (_i, []),
     "mtp_set_attn_kernel": (_i, [_i]),
     "mtp_attn_kernel": (_i, []),
+    "mtp_set_decode_kernel": (_i, [_i]),
+    "mtp_decode_kernel": (_i, []),
     "mtp_gemm_streamk_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "mtp_gemm_streamk_plan": (_i, [_i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_i64)]),
     "mtp_gemm_streamk_check": (_i, [_i64, _i64, _i64, _i, _i, _i]),
@@ -227,6 +229,16 @@ def attn_kernel() -> int:
 def set_attn_kernel(version: int) -> None:
     """1 = the 128-key tree-attention kernel, 2 = the 64-key kernel."""
     check(lib().mtp_set_attn_kernel(int(version)), "mtp_set_attn_kernel")
+
+
+def decode_kernel() -> int:
+    return int(lib().mtp_decode_kernel())
+
+
+def set_decode_kernel(version: int) -> None:
+    """Single-query attention kernel: 1 = one warp per key, 2 = 16-byte loads
+    with several keys in flight (16-bit K/V, power-of-two head size <= 256)."""
+    check(lib().mtp_set_decode_kernel(int(version)), "mtp_set_decode_kernel")
 
 
 def streamk_bytes(M: int, N: int, K: int, ab_code: int) -> int:

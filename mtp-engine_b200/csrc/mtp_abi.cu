@@ -25,6 +25,7 @@
 #include "mtp_rowattn.cuh"
 #include "mtp_kvwrite.cuh"
 #include "mtp_int4.cuh"
+#include "mtp_sqattn.cuh"
 #include "mtp_verify.cuh"
 
 using namespace mtp;
@@ -853,9 +854,77 @@ int mtp_paged_kv_write(void* k_pages, void* v_pages, int dtype, const int32_t* p
 }
 
 // ---------------------------------------------------------------- attention
+// Single-query kernel for fused_tree_attention / fused_paged_attention: 1 =
+// decode_attention_kernel (default), 2 = sq_attention_kernel where it applies
+// (16-bit K/V, D a power of two in [8, 256], 16-byte-aligned rows, scores and
+// offsets of all L keys in shared memory).  Initial value from
+// MTP_DECODE_KERNEL=2; mtp_set_decode_kernel changes it.
+static std::atomic<int> g_decode_kernel{0};
+
+static int decode_kernel_version() {
+  int v = g_decode_kernel.load(std::memory_order_relaxed);
+  if (v == 0) {
+    const char* e = getenv("MTP_DECODE_KERNEL");
+    v = (e && e[0] == '2' && e[1] == 0) ? 2 : 1;
+    int expected = 0;
+    g_decode_kernel.compare_exchange_strong(expected, v);
+    v = g_decode_kernel.load(std::memory_order_relaxed);
+  }
+  return v;
+}
+
+static bool sq_eligible(const AttnArgs& a) {
+  if (a.kind != ATTN_CONTIG && a.kind != ATTN_PAGED) return false;
+  if (a.T != 1 || a.Hq != a.Hkv || a.kv_custom || !is16bit(a.dtype)) return false;
+  if (a.D < 8 || a.D > sq::kMaxD || (a.D & (a.D - 1)) != 0) return false;
+  if (a.L > INT32_MAX / 2 || sq::smem_bytes(a.L, a.D) > 227 * 1024) return false;
+  const void* k = a.kind == ATTN_PAGED ? a.k_pages : a.k;
+  const void* v = a.kind == ATTN_PAGED ? a.v_pages : a.v;
+  return aligned16(a.q) && aligned16(a.out) && (a.L == 0 || (aligned16(k) && aligned16(v)));
+}
+
+static int launch_sq_attention(const AttnArgs& a, cudaStream_t s) {
+  sq::Args g{};
+  g.q = a.q;
+  g.out = a.out;
+  g.B = a.B;
+  g.H = a.Hq;
+  g.D = a.D;
+  g.scale = a.scale;
+  g.L = a.L;
+  g.paged = a.kind == ATTN_PAGED ? 1 : 0;
+  g.k = g.paged ? a.k_pages : a.k;
+  g.v = g.paged ? a.v_pages : a.v;
+  g.mask = a.mask;
+  g.page_table = a.page_table;
+  g.table_stride = a.table_stride;
+  g.num_pages = a.num_pages;
+  g.page_size = a.page_size;
+  const size_t smem = sq::smem_bytes(a.L, a.D);
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  static size_t attr[2][kMaxDevices] = {};
+  const int which = a.dtype == MTP_DTYPE_BF16 ? 0 : 1;
+  if (smem > 48 * 1024 && attr[which][dev] < smem) {
+    if (which == 0)
+      MTP_CUDA_TRY(cudaFuncSetAttribute(sq::sq_attention_kernel<__nv_bfloat16>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    else
+      MTP_CUDA_TRY(cudaFuncSetAttribute(sq::sq_attention_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem));
+    attr[which][dev] = smem;
+  }
+  const unsigned rows = (unsigned)(a.B * a.Hq);
+  if (which == 0) sq::sq_attention_kernel<__nv_bfloat16><<<rows, sq::kThreads, smem, s>>>(g);
+  else sq::sq_attention_kernel<__half><<<rows, sq::kThreads, smem, s>>>(g);
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
 static int launch_decode_attention(const AttnArgs& a, cudaStream_t s) {
   const int64_t rows = a.B * a.T * a.Hq;
   if (rows == 0) return MTP_OK;
+  if (rows <= INT32_MAX && decode_kernel_version() == 2 && sq_eligible(a)) return launch_sq_attention(a, s);
   if (a.D > 32 * kAttnMaxDPerLane) return fail(MTP_ERR_SHAPE, "head_dim %lld > 256", (long long)a.D);
   if (rows > INT32_MAX) return fail(MTP_ERR_SHAPE, "too many query rows");
   decode_attention_kernel<<<(unsigned)rows, 128, 0, s>>>(a);
@@ -1176,6 +1245,14 @@ int mtp_set_attn_kernel(int version) {
 }
 
 int mtp_attn_kernel(void) { return attn_kernel_version(); }
+
+int mtp_set_decode_kernel(int version) {
+  if (version != 1 && version != 2) return fail(MTP_ERR_ARG, "decode kernel %d (expected 1 or 2)", version);
+  g_decode_kernel.store(version, std::memory_order_relaxed);
+  return MTP_OK;
+}
+
+int mtp_decode_kernel(void) { return decode_kernel_version(); }
 
 size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
                                           int64_t ctx_len) {

@@ -163,3 +163,17 @@ def test_key_packing_matches_oracle():
     v = np.unique(rng.standard_normal(300).astype(np.float32))
     kk = O.pack_key(v, np.zeros(v.size, np.uint32))
     assert np.all(np.diff(kk) > 0)
+
+
+def test_decode_kernel_switch_roundtrip():
+    import _mtp_native as N
+    before = N.decode_kernel()
+    assert before in (1, 2)
+    try:
+        N.set_decode_kernel(2)
+        assert N.decode_kernel() == 2
+        N.set_decode_kernel(1)
+        assert N.decode_kernel() == 1
+        assert N.lib().mtp_set_decode_kernel(0) == 8  # MTP_ERR_ARG
+    finally:
+        N.set_decode_kernel(before)

@@ -26,6 +26,7 @@ CHILDREN = {
     "verify_step": (["test_verify_step.py"], {}, None),
     "graphs": (["test_gpu_graphs.py"], {}, None),
     "canary": (["test_gpu_canary.py"], {}, None),
+    "single_query_kernel": (["test_gpu_sqattn.py"], {}, None),
     "attention_64key_kernel": (["test_gpu_attention_tc.py", "test_gpu_parity.py"], {"MTP_ATTN_KERNEL": "2"},
                                "attention or edge_cases or device_status"),
 }
