@@ -21,14 +21,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CHILDREN = {
     "streamk": (["test_gpu_streamk.py"], {}, None),
     "tree_attn_rmsnorm_linear": (["test_gpu_tree_attn_rmsnorm_linear.py"], {}, None),
-    "paged_kv_write": (["test_paged_kv_write.py"], {}, None),
-    "quant_attention_int4": (["test_quant_attention_int4.py"], {}, None),
-    "verify_step": (["test_verify_step.py"], {}, None),
-    "graphs": (["test_gpu_graphs.py"], {}, None),
-    "canary": (["test_gpu_canary.py"], {}, None),
-    "single_query_kernel": (["test_gpu_sqattn.py"], {}, None),
     "attention_64key_kernel": (["test_gpu_attention_tc.py", "test_gpu_parity.py"], {"MTP_ATTN_KERNEL": "2"},
                                "attention or edge_cases or device_status"),
+    # smaller operators and whole-path checks, one child for all of them
+    "operators": (["test_verify_step.py", "test_paged_kv_write.py", "test_quant_attention_int4.py",
+                   "test_gpu_sqattn.py", "test_gpu_graphs.py", "test_gpu_canary.py"], {}, None),
 }
 
 
@@ -38,7 +35,7 @@ def test_child(name):
         pytest.skip("no CUDA device")
     files, extra, kexpr = CHILDREN[name]
     env = dict(os.environ, MTP_ISOLATED_RUN="1", **extra)
-    cmd = [sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider"]
+    cmd = [sys.executable, "-m", "pytest", "-q", "-m", "gpu", "-p", "no:cacheprovider"]
     if kexpr:
         cmd += ["-k", kexpr]
     cmd += [os.path.join(HERE, f) for f in files]
