@@ -40,5 +40,5 @@ def test_child(name):
         cmd += ["-k", kexpr]
     cmd += [os.path.join(HERE, f) for f in files]
     r = subprocess.run(cmd, env=env, cwd=os.path.dirname(HERE), capture_output=True, text=True, timeout=1200)
-    tail = "\n".join((r.stdout + r.stderr).strip().splitlines()[-25:])
+    tail = "\n".join((r.stdout + r.stderr).strip().splitlines()[-40:])
     assert r.returncode == 0, f"child pytest for {name} exited {r.returncode}:\n{tail}"
