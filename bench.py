@@ -145,7 +145,7 @@ def run_ours(args):
     import mtp_fused_verify as mv
     import mtp_kernels as mk
     import mtp_parallel as mp
-    from oracle import mtp_oracle as O  # used only for the reported CPU baseline and draft setup
+    from mtp_draft_tree import SpeculativeDraftTree
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -175,9 +175,10 @@ def run_ours(args):
     per_seq = ctx // ps
     table = torch.stack([perm[b * per_seq:(b + 1) * per_seq].repeat_interleave(ps) for b in range(B4)])
     table = table.to(torch.int32).to(dev)
-    _, tmask_np = O.draft_tree(C4["depth"], C4["branches"], "tree")
+    tmask_t = SpeculativeDraftTree(C4["depth"], C4["branches"], "tree").tree_mask
+    tmask_np = tmask_t.numpy()
     T = tmask_np.shape[0]
-    tmask = torch.tensor(tmask_np, device=dev)
+    tmask = tmask_t.to(dev)
     q = torch.randn(B4, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
     tk = torch.randn(B4, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
     tv = torch.randn(B4, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
@@ -193,7 +194,7 @@ def run_ours(args):
                                           B5 * S5, K5, hi - lo, lo, N.stream_handle(dev)), "setup keys")
     if world > 1:
         dist.all_reduce(keys, op=dist.ReduceOp.MAX)
-    top = O.key_index(keys.cpu().numpy()).reshape(B5, S5)
+    top = mp.key_index(keys).cpu().numpy().reshape(B5, S5)
     rng = np.random.default_rng(4)
     draft_np = rng.integers(0, V5, size=(B5, S5 - 1))
     for b in range(B5):
@@ -536,7 +537,8 @@ def run_sweep(args):
     import _mtp_native as N
     import mtp_fused_verify as mv
     import mtp_kernels as mk
-    from oracle import mtp_oracle as O
+    from mtp_draft_tree import SpeculativeDraftTree
+    from oracle import mtp_oracle as O  # the CPU-baseline column of each line only
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -637,7 +639,7 @@ def run_sweep(args):
     del x, xq, wq
     # ---- config 4: paged tree attention
     B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
-    _, tm = O.draft_tree(C4["depth"], C4["branches"], "tree")
+    tm = SpeculativeDraftTree(C4["depth"], C4["branches"], "tree").tree_mask.numpy()
     T = tm.shape[0]
     g = torch.Generator(device=dev).manual_seed(3)
     kp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
@@ -770,6 +772,58 @@ def run_sweep(args):
     assert N.device_status(dev) == 0
 
 
+def run_profile_case(args):
+    """--profile-case: one operator at its BASELINE config, called --steps
+    times with CUDA-event timing printed per call -- the small, fixed
+    workload the ncu captures in profiles/ are taken on."""
+    import torch
+
+    import mtp_fused_verify as mv
+    import mtp_kernels as mk
+    from mtp_draft_tree import SpeculativeDraftTree
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    case = args.profile_case
+    if case == "attention":
+        B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
+        tm = SpeculativeDraftTree(C4["depth"], C4["branches"], "tree").tree_mask.numpy()
+        T = tm.shape[0]
+        g = torch.Generator(device=dev).manual_seed(3)
+        kp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
+        vp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
+        perm = torch.randperm(P, generator=torch.Generator().manual_seed(3))
+        per = ctx // ps
+        table = torch.stack([perm[b * per:(b + 1) * per].repeat_interleave(ps) for b in range(B)])
+        table = table.to(torch.int32).to(dev)
+        q = torch.randn(B, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+        tk = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+        tv = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+        tmask = torch.tensor(tm, device=dev)
+        fn = lambda: mk.fused_tree_attention_paged(q, kp, vp, table, tk, tv, tmask)
+    else:
+        g = torch.Generator(device=dev).manual_seed(4)
+        if case == "verify":
+            B, S, K, V = C5["B"], C5["S"], C5["K"], C5["V"]
+            hid = torch.randn(B, S, K, generator=g, device=dev).to(torch.bfloat16)
+            w = (0.02 * torch.randn(V, K, generator=g, device=dev)).to(torch.bfloat16)
+            d = torch.randint(0, V, (B, S - 1), device=dev, dtype=torch.int32)
+            fn = lambda: mv.fused_multi_verify(hid, w, d)
+        else:  # rms
+            M, K, Nn = C2["M"], C2["K"], C2["N"]
+            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            gam = 1 + 0.1 * torch.randn(K, generator=g, device=dev)
+            w = (0.02 * torch.randn(Nn, K, generator=g, device=dev)).to(torch.bfloat16)
+            fn = lambda: mk.fused_rmsnorm_linear(x, w, None, 1e-5, norm_weight=gam)
+    for i in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"{case} call {i}: {e0.elapsed_time(e1) * 1000:.1f} us", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -784,6 +838,9 @@ def main():
     ap.add_argument("--exchange", choices=["nccl", "p2p", "fused"], default="nccl",
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
                          "or the all-reduce fused into the shard GEMM")
+    ap.add_argument("--profile-case", choices=["verify", "rms", "attention"], default=None,
+                    help="call one operator at its BASELINE config --steps times (the workload of the ncu "
+                         "captures in profiles/)")
     ap.add_argument("--compare", action="store_true",
                     help="with --sweep: every GEMM config under both schedules, config 4 under both attention "
                          "kernels, the single-query lines under both decode kernels")
@@ -792,7 +849,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.sweep:
         run_sweep(args)

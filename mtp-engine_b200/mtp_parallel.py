@@ -110,6 +110,12 @@ def vocab_shard_range(vocab_size: int, world: int, rank: int) -> Tuple[int, int]
     return lo, min(lo + step, vocab_size)
 
 
+def key_index(keys: torch.Tensor) -> torch.Tensor:
+    """Global vocabulary index carried in the low 32 bits of packed row keys
+    (int64 -> int32, on the keys' device)."""
+    return (0xFFFFFFFF - (keys & 0xFFFFFFFF)).to(torch.int32)
+
+
 def shard_lm_head(weight: torch.Tensor, world: int, rank: int) -> Tuple[torch.Tensor, int]:
     """This rank's contiguous vocabulary block of a full lm_head and its offset."""
     lo, hi = vocab_shard_range(weight.shape[0], world, rank)

@@ -75,6 +75,9 @@ def main():
     if args.only == "quant_attention_int4":
         make_quant_attention_int4(torch, mk)
         return
+    if args.only == "draft_tree":
+        make_draft_trees(SpeculativeDraftTree)
+        return
     if args.only == "paged_kv_write":
         import mtp_engine
         make_paged_kv_write(torch, mtp_engine)
@@ -272,19 +275,35 @@ def main():
          tree_k=f32(tk), tree_v=f32(tv), tree_mask=f32(tree.tree_mask),
          meta=np.array([ctx, pst], dtype=np.int64), out=f32(out_t))
 
-    # ---------------------------------------------------------------- draft trees
-    arrs = {}
-    for (dep, br, mode) in [(16, 4, "tree"), (4, 8, "tree"), (4, 8, "trunk"), (4, 2, "tree")]:
-        t = SpeculativeDraftTree(depth=dep, max_branches=br, mode=mode)
-        key = f"{mode}_{dep}_{br}"
-        arrs[key + "_parent"] = t.parent.numpy()
-        arrs[key + "_mask"] = t.tree_mask.numpy()
-    save("draft_tree.npz", **arrs)
-
+    make_draft_trees(SpeculativeDraftTree)
     make_tree_attn_rmsnorm_linear(torch, mk)
     import mtp_engine
     make_paged_kv_write(torch, mtp_engine)
     make_quant_attention_int4(torch, mk)
+
+
+# (depth, max_branches, mode): the config-4 tree, small trees, trees whose
+# node budget runs out inside a level (3*8: level 2 gets 15 of 64 children),
+# chains, and single-branch trees
+DRAFT_TREES = [(16, 4, "tree"), (4, 8, "tree"), (4, 8, "trunk"), (4, 2, "tree"), (3, 8, "tree"),
+               (5, 3, "tree"), (8, 4, "tree"), (1, 4, "tree"), (1, 1, "trunk"), (6, 1, "tree"),
+               (7, 2, "trunk"), (2, 3, "tree")]
+
+
+def make_draft_trees(SpeculativeDraftTree):
+    """SpeculativeDraftTree (mtp_engine.py:635-719): parent index, ancestor
+    mask, linear layout and active node count."""
+    arrs = {}
+    for (dep, br, mode) in DRAFT_TREES:
+        t = SpeculativeDraftTree(depth=dep, max_branches=br, mode=mode)
+        key = f"{mode}_{dep}_{br}"
+        arrs[key + "_parent"] = t.parent.numpy()
+        arrs[key + "_mask"] = t.tree_mask.numpy()
+        do, bo = t.build_linear_layout()
+        arrs[key + "_depth_offsets"] = do.numpy()
+        arrs[key + "_branch_offsets"] = bo.numpy()
+        arrs[key + "_active"] = np.array(t.active_node_count(), dtype=np.int64)
+    save("draft_tree.npz", **arrs)
 
 
 def make_quant_attention_int4(torch, mk):
