@@ -158,6 +158,11 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     prim = mp.get_parallel_primitives()
     assert C2["N"] % world == 0 and C4["Hkv"] % world == 0
+    comm = None  # --exchange abi: the library's own NCCL communicator (C ABI)
+    if world > 1 and args.exchange == "abi":
+        uid = [mp.NcclCommunicator.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = mp.NcclCommunicator(uid[0], rank, world, dev)
 
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     # ---- stage 1 inputs (columns split)
@@ -214,6 +219,8 @@ def run_ours(args):
     def stage3(hh, dd):
         if world == 1:
             return mv.fused_multi_verify(hh, lm, dd)
+        if comm is not None:
+            return mp.vocab_parallel_multi_verify_nccl(hh, lm, dd, lo, comm)
         return mp.vocab_parallel_multi_verify(hh, lm, dd, None, lo, prim, exchange=args.exchange)
 
     def barrier():
@@ -363,6 +370,9 @@ def run_ours(args):
     import gc
     gc.collect()
     torch.cuda.synchronize(dev)
+    if comm is not None:  # after the graphs that may hold its all-reduce
+        comm.close()
+        comm = None
     if rank != 0:
         if world > 1:
             dist.barrier(device_ids=[local])
@@ -412,7 +422,8 @@ def run_ours(args):
                    "seq_len": C5["S"],
                    "parallelism": "tp1" if world == 1 else f"tp{world} (cols / kv-heads / vocab)",
                    "l2": "inputs larger than L2 (about 2.3 GB touched per step)",
-                   "gemm_schedule": args.gemm_schedule},
+                   "gemm_schedule": args.gemm_schedule,
+                   "exchange": args.exchange if world > 1 else "none"},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -835,9 +846,10 @@ def main():
     ap.add_argument("--graph", action="store_true", help="also replay captured graphs when n_gpus > 1")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--sweep", action="store_true", help="time every BASELINE config on its own (1 GPU)")
-    ap.add_argument("--exchange", choices=["nccl", "p2p", "fused"], default="nccl",
+    ap.add_argument("--exchange", choices=["nccl", "p2p", "fused", "abi"], default="nccl",
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
-                         "or the all-reduce fused into the shard GEMM")
+                         "the all-reduce fused into the shard GEMM, or the one-call C-ABI verify over the "
+                         "library's own NCCL communicator")
     ap.add_argument("--profile-case", choices=["verify", "rms", "attention"], default=None,
                     help="call one operator at its BASELINE config --steps times (the workload of the ncu "
                          "captures in profiles/)")

@@ -46,6 +46,7 @@ extern "C" {
 #define MTP_ERR_WORKSPACE 6   /* workspace missing or too small */
 #define MTP_ERR_DEVICE 7      /* a device-side check failed */
 #define MTP_ERR_ARG 8         /* null pointer or bad scalar argument */
+#define MTP_ERR_NCCL 9        /* NCCL missing, or an NCCL call failed */
 
 /* ABI version of this header (bumped on any signature change). */
 int mtp_abi_version(void);
@@ -325,6 +326,65 @@ int mtp_verify_shard_keys_ws(const void* hidden, int h_dtype, const void* weight
 int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* accept,
                                int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S,
                                void* stream);
+
+/* ---- NCCL communicator for C hosts -------------------------------------
+ * The reference's vocab-parallel exchange is a torch process group
+ * (ParallelPrimitives, mtp_parallel.py:12-66; RowParallelLinear's gather,
+ * mtp_parallel.py:114-118).  A host without torch.distributed creates one
+ * NCCL communicator per rank with these calls and passes it to
+ * mtp_vocab_parallel_multi_verify.  NCCL is opened at run time
+ * (libnccl.so.2, or the file named by the MTP_NCCL_LIBRARY environment
+ * variable; a copy the process already loaded is reused); when it cannot be
+ * opened these calls return MTP_ERR_NCCL and the rest of the library is
+ * unaffected. */
+#define MTP_NCCL_ID_BYTES 128
+
+/* NCCL's version code (e.g. 22809 for 2.28.9) in *version. */
+int mtp_nccl_version(int* version);
+
+/* ncclGetUniqueId: rank 0 makes the id and the host sends its
+ * MTP_NCCL_ID_BYTES bytes to every rank. */
+int mtp_nccl_unique_id(void* id);
+
+/* ncclCommInitRank on the current CUDA device (mtp_nccl_init of the
+ * boundary): collective, returns once all `world` ranks have joined.
+ * *comm receives an opaque handle. */
+int mtp_nccl_comm_init(void** comm, const void* id, int rank, int world);
+
+/* ncclCommDestroy (comm may be NULL). */
+int mtp_nccl_comm_destroy(void* comm);
+
+/* ncclCommAbort: ends a communicator whose collective cannot finish (a
+ * rank died) without waiting for it, e.g. from a host thread that watches a
+ * stream the collective holds.  The handle is freed, as by destroy; no
+ * other call may be using it. */
+int mtp_nccl_comm_abort(void* comm);
+
+/* ncclCommGetAsyncError: MTP_OK, or MTP_ERR_NCCL with NCCL's error text. */
+int mtp_nccl_comm_status(void* comm);
+
+/* Workspace of mtp_vocab_parallel_multi_verify: the keys [B*S] int64 (a
+ * multiple of 256 bytes) followed by mtp_gemm_streamk_bytes(B*S, V_shard,
+ * K, h_dtype) bytes for the shard GEMM's stream-K schedule.  Fill it once
+ * with mtp_keys_fill over all of it; every successful call leaves it so. */
+size_t mtp_vocab_parallel_workspace(int64_t B, int64_t S, int64_t V_shard, int64_t K, int h_dtype);
+
+/* One rank's vocab-parallel fused_multi_verify in one call: this rank's
+ * block [vocab_offset, vocab_offset + V_shard) of the lm_head folded into
+ * argmax keys (mtp_verify_shard_keys_ws), the keys all-reduced with MAX
+ * over `comm` (ncclInt64, in place; no collective when comm is NULL, a
+ * single-rank run), then decoded into accept [B, S-1] int8, accepted_n [B]
+ * and corrected [B] int32 -- identical on every rank and equal to
+ * mtp_fused_multi_verify over the whole lm_head (mtp_fused_verify.py:
+ * 237-290 with the weight split as torch.chunk splits it,
+ * mtp_parallel.py:62-66).  The current device must be the communicator's.
+ * After MTP_ERR_NCCL or MTP_ERR_TIMEOUT the keys may be mid-reduction: fill
+ * the workspace again before the next call. */
+int mtp_vocab_parallel_multi_verify(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                                    const void* bias_shard, int bias_dtype, const int32_t* draft,
+                                    int8_t* accept, int32_t* accepted_n, int32_t* corrected, int64_t B,
+                                    int64_t S, int64_t K, int64_t V_shard, int64_t vocab_offset, void* comm,
+                                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* Largest B*S that mtp_fused_multi_verify_noalloc accepts. */
 #define MTP_NOALLOC_MAX_ROWS 8192

@@ -24,7 +24,9 @@ if hasattr(torch, "float8_e4m3fn"):
     _DTYPE_CODES[torch.float8_e4m3fn] = DT_E4M3
 
 STATUS_NAMES = {0: "OK", 1: "MTP_ERR_SHAPE", 2: "MTP_ERR_DTYPE", 3: "MTP_ERR_ALIGN", 4: "MTP_ERR_CUDA",
-                5: "MTP_ERR_TIMEOUT", 6: "MTP_ERR_WORKSPACE", 7: "MTP_ERR_DEVICE", 8: "MTP_ERR_ARG"}
+                5: "MTP_ERR_TIMEOUT", 6: "MTP_ERR_WORKSPACE", 7: "MTP_ERR_DEVICE", 8: "MTP_ERR_ARG",
+                9: "MTP_ERR_NCCL"}
+NCCL_ID_BYTES = 128
 
 _vp, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
@@ -60,6 +62,15 @@ SIGNATURES = {
     "mtp_verify_shard_keys_ws": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
+    "mtp_nccl_version": (_i, [ctypes.POINTER(_i)]),
+    "mtp_nccl_unique_id": (_i, [_vp]),
+    "mtp_nccl_comm_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i]),
+    "mtp_nccl_comm_destroy": (_i, [_vp]),
+    "mtp_nccl_comm_abort": (_i, [_vp]),
+    "mtp_nccl_comm_status": (_i, [_vp]),
+    "mtp_vocab_parallel_workspace": (_sz, [_i64, _i64, _i64, _i64, _i]),
+    "mtp_vocab_parallel_multi_verify": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                             _i64, _i64, _vp, _vp, _sz, _vp]),
     "mtp_verify_step": (_i, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "mtp_verify_fused_bytes": (_sz, [_i64, _i]),
     "mtp_verify_fused_init": (_i, [_vp, _i64, _i, _vp]),

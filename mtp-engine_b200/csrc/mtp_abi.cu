@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <new>
 #include <vector>
 #include <stdarg.h>
 #include <stdlib.h>
@@ -24,6 +25,7 @@
 #include "mtp_rownorm.cuh"
 #include "mtp_rowattn.cuh"
 #include "mtp_kvwrite.cuh"
+#include "mtp_nccl.cuh"
 #include "mtp_int4.cuh"
 #include "mtp_sqattn.cuh"
 #include "mtp_verify.cuh"
@@ -1617,6 +1619,126 @@ int mtp_verify_chain_from_keys(int64_t* keys, const int32_t* draft, int8_t* acce
   verify_finalize_kernel<<<blocks, 128, 0, as_stream(stream)>>>(ep);
   MTP_LAUNCH_CHECK();
   return MTP_OK;
+}
+
+// ---- NCCL communicator for C hosts ------------------------------------------
+
+#define MTP_NCCL_TRY(expr)                                                                        \
+  do {                                                                                            \
+    ncclResult_t r_ = (expr);                                                                     \
+    if (r_ != ncclSuccess) return fail(MTP_ERR_NCCL, "%s: %s", #expr, nccl::error_string(r_));   \
+  } while (0)
+
+static int nccl_loaded() {
+  const nccl::Api& a = nccl::api();
+  return a.ok ? MTP_OK : fail(MTP_ERR_NCCL, "%s", a.why);
+}
+
+int mtp_nccl_version(int* version) {
+  if (!version) return fail(MTP_ERR_ARG, "null version");
+  if (int st = nccl_loaded()) return st;
+  *version = nccl::api().version;
+  return MTP_OK;
+}
+
+int mtp_nccl_unique_id(void* id) {
+  if (!id) return fail(MTP_ERR_ARG, "null id");
+  if (int st = nccl_loaded()) return st;
+  ncclUniqueId u;
+  MTP_NCCL_TRY(nccl::api().GetUniqueId(&u));
+  memcpy(id, &u, sizeof(u));
+  return MTP_OK;
+}
+
+int mtp_nccl_comm_init(void** comm, const void* id, int rank, int world) {
+  if (!comm || !id) return fail(MTP_ERR_ARG, "null comm or id");
+  *comm = nullptr;
+  if (world < 1 || rank < 0 || rank >= world) return fail(MTP_ERR_ARG, "rank %d of world %d", rank, world);
+  if (int st = nccl_loaded()) return st;
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof(u));
+  ncclComm_t c = nullptr;
+  MTP_NCCL_TRY(nccl::api().CommInitRank(&c, world, u, rank));
+  nccl::Comm* h = new (std::nothrow) nccl::Comm;
+  if (!h) {
+    nccl::api().CommDestroy(c);
+    return fail(MTP_ERR_ARG, "out of host memory");
+  }
+  h->comm = c;
+  h->rank = rank;
+  h->world = world;
+  h->device = dev;
+  *comm = h;
+  return MTP_OK;
+}
+
+int mtp_nccl_comm_destroy(void* comm) {
+  if (!comm) return MTP_OK;
+  nccl::Comm* h = static_cast<nccl::Comm*>(comm);
+  if (int st = nccl_loaded()) return st;
+  const ncclResult_t r = nccl::api().CommDestroy(h->comm);
+  delete h;
+  return r == ncclSuccess ? MTP_OK : fail(MTP_ERR_NCCL, "ncclCommDestroy: %s", nccl::error_string(r));
+}
+
+int mtp_nccl_comm_abort(void* comm) {
+  if (!comm) return MTP_OK;
+  nccl::Comm* h = static_cast<nccl::Comm*>(comm);
+  if (int st = nccl_loaded()) return st;
+  const ncclResult_t r = nccl::api().CommAbort(h->comm);  // frees the NCCL communicator
+  delete h;
+  return r == ncclSuccess ? MTP_OK : fail(MTP_ERR_NCCL, "ncclCommAbort: %s", nccl::error_string(r));
+}
+
+int mtp_nccl_comm_status(void* comm) {
+  if (!comm) return fail(MTP_ERR_ARG, "null comm");
+  if (int st = nccl_loaded()) return st;
+  ncclResult_t async = ncclSuccess;
+  MTP_NCCL_TRY(nccl::api().CommGetAsyncError(static_cast<nccl::Comm*>(comm)->comm, &async));
+  return async == ncclSuccess ? MTP_OK : fail(MTP_ERR_NCCL, "NCCL: %s", nccl::error_string(async));
+}
+
+size_t mtp_vocab_parallel_workspace(int64_t B, int64_t S, int64_t V_shard, int64_t K, int h_dtype) {
+  if (B < 0 || S < 1 || V_shard < 0 || K < 0) return 0;
+  const int64_t rows = B * S;
+  const size_t keys = align256((size_t)(rows > 0 ? rows : 1) * 8);
+  return keys + (rows > 0 && V_shard > 0 && K > 0 ? mtp_gemm_streamk_bytes(rows, V_shard, K, h_dtype) : 0);
+}
+
+int mtp_vocab_parallel_multi_verify(const void* hidden, int h_dtype, const void* weight_shard, int w_dtype,
+                                    const void* bias_shard, int bias_dtype, const int32_t* draft,
+                                    int8_t* accept, int32_t* accepted_n, int32_t* corrected, int64_t B,
+                                    int64_t S, int64_t K, int64_t V_shard, int64_t vocab_offset, void* comm,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  MTP_NVTX("mtp_vocab_parallel_multi_verify");
+  if (B < 0 || S < 1 || K < 0 || V_shard < 0) return fail(MTP_ERR_SHAPE, "bad verify sizes");
+  if (B == 0) return MTP_OK;
+  const int64_t rows = B * S;
+  const size_t keys_bytes = align256((size_t)rows * 8);
+  if (!workspace || workspace_bytes < keys_bytes)
+    return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", keys_bytes);
+  if (!aligned16(workspace)) return fail(MTP_ERR_ALIGN, "workspace not 16-byte aligned");
+  const nccl::Comm* c = static_cast<const nccl::Comm*>(comm);
+  if (c) {
+    if (int st = nccl_loaded()) return st;
+    int dev;
+    if (int st = current_device(&dev)) return st;
+    if (dev != c->device) return fail(MTP_ERR_ARG, "current device %d, communicator on device %d", dev, c->device);
+  }
+  int64_t* keys = static_cast<int64_t*>(workspace);
+  cudaStream_t s = as_stream(stream);
+  // an empty block contributes no key: its rank's keys stay at INT64_MIN
+  if (V_shard > 0) {
+    if (int st = mtp_verify_shard_keys_ws(hidden, h_dtype, weight_shard, w_dtype, bias_shard, bias_dtype, keys,
+                                          rows, K, V_shard, vocab_offset, static_cast<uint8_t*>(workspace) + keys_bytes,
+                                          workspace_bytes - keys_bytes, stream))
+      return st;
+  }
+  if (c && c->world > 1)
+    MTP_NCCL_TRY(nccl::api().AllReduce(keys, keys, (size_t)rows, ncclInt64, ncclMax, c->comm, s));
+  return mtp_verify_chain_from_keys(keys, draft, accept, accepted_n, corrected, B, S, stream);
 }
 
 }  // extern "C"

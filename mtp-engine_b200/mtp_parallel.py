@@ -293,6 +293,108 @@ def vocab_parallel_multi_verify(
     return accept, accepted_n, corrected
 
 
+class NcclCommunicator:
+    """One rank's NCCL communicator made through the C ABI
+    (mtp_nccl_comm_init), for processes that run the vocab-parallel verify
+    without a torch.distributed process group.  Rank 0 calls ``unique_id()``
+    and the host sends those bytes to every rank (any transport); each rank
+    then builds ``NcclCommunicator(uid, rank, world)`` with its own GPU
+    current.  The constructor returns once every rank has joined."""
+
+    def __init__(self, uid: bytes, rank: int, world: int, device: Optional[torch.device] = None):
+        if len(uid) != _N.NCCL_ID_BYTES:
+            raise ValueError(f"unique id must be {_N.NCCL_ID_BYTES} bytes, got {len(uid)}")
+        self.rank, self.world = int(rank), int(world)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        self._h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _N.check(_N.lib().mtp_nccl_comm_init(ctypes.byref(self._h), ctypes.create_string_buffer(uid, len(uid)),
+                                                 self.rank, self.world), "mtp_nccl_comm_init")
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(_N.NCCL_ID_BYTES)
+        _N.check(_N.lib().mtp_nccl_unique_id(buf), "mtp_nccl_unique_id")
+        return buf.raw
+
+    @staticmethod
+    def version() -> int:
+        v = ctypes.c_int(0)
+        _N.check(_N.lib().mtp_nccl_version(ctypes.byref(v)), "mtp_nccl_version")
+        return v.value
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if not self._h:
+            raise RuntimeError("communicator is closed")
+        return self._h
+
+    def status(self) -> None:
+        """Raises RuntimeError when NCCL reports an asynchronous error."""
+        _N.check(_N.lib().mtp_nccl_comm_status(self.handle), "mtp_nccl_comm_status")
+
+    def abort(self) -> None:
+        """End the communicator without waiting for its collectives (a rank
+        died); the communicator cannot be used afterwards."""
+        if self._h:
+            h, self._h = self._h, ctypes.c_void_p()
+            _N.check(_N.lib().mtp_nccl_comm_abort(h), "mtp_nccl_comm_abort")
+
+    def close(self) -> None:
+        if self._h:
+            h, self._h = self._h, ctypes.c_void_p()
+            _N.check(_N.lib().mtp_nccl_comm_destroy(h), "mtp_nccl_comm_destroy")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+_ABI_WS = "vocab_parallel_abi"
+
+
+def vocab_parallel_multi_verify_nccl(
+    hidden: torch.Tensor, weight_shard: torch.Tensor, draft: torch.Tensor, vocab_offset: int,
+    comm: Optional[NcclCommunicator], bias_shard: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """vocab_parallel_multi_verify over a C-ABI NCCL communicator: one call
+    of mtp_vocab_parallel_multi_verify (shard GEMM to argmax keys, NCCL
+    all-reduce(MAX) of the keys, acceptance scan).  ``comm=None`` is a
+    single-rank run.  Returns the replicated (accept, accepted_n, corrected)
+    of fused_multi_verify on the whole lm_head."""
+    if hidden.dim() != 3 or draft.dim() != 2:
+        raise ValueError("hidden must be [B, S, K] and draft [B, S-1]")
+    B, S, K = hidden.shape
+    assert S == draft.shape[1] + 1, "hidden.shape[1] must equal draft.shape[1] + 1"
+    assert weight_shard.shape[1] == K, "weight_shard must be [V_shard, K]"
+    dev = _N.require_cuda(hidden, weight_shard, draft, bias_shard)
+    hidden = hidden.contiguous()
+    weight_shard = weight_shard.contiguous()
+    draft = draft.contiguous().to(torch.int32)
+    if bias_shard is not None:
+        bias_shard = bias_shard.contiguous()
+    Vr = weight_shard.shape[0]
+    accept = torch.empty((B, S - 1), dtype=torch.int8, device=dev)
+    accepted_n = torch.empty((B,), dtype=torch.int32, device=dev)
+    corrected = torch.empty((B,), dtype=torch.int32, device=dev)
+    L = _N.lib()
+    need = L.mtp_vocab_parallel_workspace(B, S, Vr, K, _N.dtype_code(hidden))
+    ws = _N.workspace(dev, _ABI_WS, need, _N._rest_fill(dev))  # every word INT64_MIN
+    try:
+        _N.check(L.mtp_vocab_parallel_multi_verify(
+            _N.ptr(hidden), _N.dtype_code(hidden), _N.ptr(weight_shard), _N.dtype_code(weight_shard),
+            _N.ptr(bias_shard), _N.dtype_code(bias_shard) if bias_shard is not None else 0, _N.ptr(draft),
+            _N.ptr(accept), _N.ptr(accepted_n), _N.ptr(corrected), B, S, K, Vr, int(vocab_offset),
+            comm.handle if comm is not None else None, _N.ptr(ws), ws.numel(), _N.stream_handle(dev)),
+            "mtp_vocab_parallel_multi_verify")
+    except Exception:
+        _N.drop_workspace(dev, _ABI_WS)  # never reuse keys left mid-reduction
+        raise
+    return accept, accepted_n, corrected
+
+
 class VocabParallelVerify:
     """Callable holding one rank's lm_head shard: ``__call__(hidden, draft)``
     returns the replicated (accept, accepted_n, corrected)."""
@@ -360,5 +462,6 @@ class RowParallelLinear(nn.Module):
 
 __all__ = [
     "ParallelPrimitives", "get_parallel_primitives", "vocab_shard_range", "shard_lm_head",
-    "vocab_parallel_multi_verify", "VocabParallelVerify", "RowParallelLinear",
+    "vocab_parallel_multi_verify", "VocabParallelVerify", "RowParallelLinear", "key_index",
+    "NcclCommunicator", "vocab_parallel_multi_verify_nccl",
 ]

@@ -1,5 +1,7 @@
-"""Vocab-parallel verify on 2+ GPUs (NCCL ranks): both key exchanges --
-the NCCL all-reduce and the peer-memory kernel -- must return exactly what
+"""Vocab-parallel verify on 2+ GPUs (NCCL ranks): every key exchange --
+the NCCL all-reduce through torch.distributed, the peer-memory kernel, the
+all-reduce fused into the shard GEMM, and the one-call C-ABI entry over its
+own NCCL communicator -- must return exactly what
 single-device fused_multi_verify returns on the full lm_head, on every rank,
 for several calls in a row.  Runs only with MTP_TEST_MULTI_GPU=1 and at least
 two visible GPUs (GPU only)."""
@@ -41,6 +43,10 @@ def _rank(rank, world, port, q):
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
         prim = mp.ParallelPrimitives()
+        # a second, C-ABI NCCL communicator: rank 0's id sent over the process group
+        uid = [mp.NcclCommunicator.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = mp.NcclCommunicator(uid[0], rank, world, dev)
         results = []
         for call in range(3):
             g = torch.Generator(device=dev).manual_seed(100 + call)  # same inputs on every rank
@@ -50,11 +56,16 @@ def _rank(rank, world, port, q):
             draft = torch.randint(0, V, (B, S - 1), generator=g, device=dev, dtype=torch.int32)
             ref = mv.fused_multi_verify(hid, w, draft)
             shard, off = mp.shard_lm_head(w, world, rank)
-            for exchange in ("nccl", "p2p", "fused"):
-                got = mp.vocab_parallel_multi_verify(hid, shard, draft, None, off, prim, exchange=exchange)
+            for exchange in ("nccl", "p2p", "fused", "abi"):
+                if exchange == "abi":
+                    got = mp.vocab_parallel_multi_verify_nccl(hid, shard, draft, off, comm)
+                else:
+                    got = mp.vocab_parallel_multi_verify(hid, shard, draft, None, off, prim, exchange=exchange)
                 torch.cuda.synchronize(dev)
                 same = all(torch.equal(a, b) for a, b in zip(got, ref))
                 results.append((call, exchange, same))
+        comm.status()
+        comm.close()
         import _mtp_native as N
         status = N.device_status(dev)
         dist.barrier(device_ids=[rank])
