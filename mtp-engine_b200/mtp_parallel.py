@@ -18,14 +18,18 @@ CPU test ranks).
 
 Also provided for drop-in compatibility: ParallelPrimitives /
 get_parallel_primitives (same properties and collectives as
-mtp_parallel.py:12-81) and RowParallelLinear (vocab-sharded linear,
-mtp_parallel.py:84-118) with an added ``verify`` method.
+mtp_parallel.py:12-81), RowParallelLinear (vocab-sharded linear,
+mtp_parallel.py:84-118) with an added ``verify`` method, and
+ColumnParallelLinear (mtp_parallel.py:121-156).
 """
 
 from __future__ import annotations
 
 import ctypes
+import importlib.util
 import math
+import os
+import sys
 from typing import List, Optional, Tuple
 
 import torch
@@ -460,8 +464,72 @@ class RowParallelLinear(nn.Module):
         return vocab_parallel_multi_verify(hidden, self.weight, draft, self.bias, off, self.prim)
 
 
+class ColumnParallelLinear(nn.Module):
+    """Linear layer whose in_features are split over the ranks, as in
+    mtp_parallel.py:121-156: forward() takes this rank's torch.chunk slice
+    of x along the last dim and returns its partial product (plus the full
+    bias), all-gathered along the last dim when gather_output.  Kept for
+    drop-in compatibility; it is not on the verify path (the verify splits the
+    vocabulary, RowParallelLinear / vocab_parallel_multi_verify)."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, gather_output: bool = False,
+                 prim: Optional[ParallelPrimitives] = None):
+        super().__init__()
+        self.prim = prim if prim is not None else get_parallel_primitives()
+        tp = self.prim.tp_size
+        assert in_features % tp == 0
+        self.in_features = in_features
+        self.in_features_per_rank = in_features // tp
+        self.out_features = out_features
+        self.gather_output = gather_output
+        self.weight = nn.Parameter(torch.empty(out_features, self.in_features_per_rank))
+        self.bias = nn.Parameter(torch.empty(out_features)) if bias else None
+        self.reset_parameters()
+
+    def reset_parameters(self) -> None:
+        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
+        if self.bias is not None:
+            bound = 1.0 / math.sqrt(self.in_features_per_rank)
+            nn.init.uniform_(self.bias, -bound, bound)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        y = F.linear(self.prim.scatter(x, dim=-1, shard_size=self.in_features_per_rank), self.weight, self.bias)
+        return self.prim.all_gather(y, dim=-1) if self.gather_output else y
+
+
+# --------------------------------------------------------------------------- #
+# names outside the hot path (SegmentedGraphRunner, GraphSegment, ...)
+# --------------------------------------------------------------------------- #
+_reference_module = None
+
+
+def _load_reference():
+    global _reference_module
+    if _reference_module is None:
+        root = os.environ.get("MTP_REFERENCE_PATH")
+        if not root:
+            return None
+        spec = importlib.util.spec_from_file_location("_mtp_reference_parallel", os.path.join(root, "mtp_parallel.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules["_mtp_reference_parallel"] = mod
+        spec.loader.exec_module(mod)
+        _reference_module = mod
+    return _reference_module
+
+
+def __getattr__(name: str):
+    if name.startswith("__"):
+        raise AttributeError(name)
+    ref = _load_reference()
+    if ref is not None and hasattr(ref, name):
+        return getattr(ref, name)
+    raise AttributeError(
+        f"mtp_parallel.{name} is not part of the B200 hot path implemented by mtp-engine-b200; "
+        "set MTP_REFERENCE_PATH to the reference checkout to resolve it there")
+
+
 __all__ = [
     "ParallelPrimitives", "get_parallel_primitives", "vocab_shard_range", "shard_lm_head",
-    "vocab_parallel_multi_verify", "VocabParallelVerify", "RowParallelLinear", "key_index",
-    "NcclCommunicator", "vocab_parallel_multi_verify_nccl",
+    "vocab_parallel_multi_verify", "VocabParallelVerify", "RowParallelLinear", "ColumnParallelLinear",
+    "key_index", "NcclCommunicator", "vocab_parallel_multi_verify_nccl",
 ]
