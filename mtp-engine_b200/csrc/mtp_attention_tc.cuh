@@ -51,6 +51,11 @@ constexpr int kMaxPagesPerChunk = 16;            // page_size >= 8
 constexpr int kSmemBytes = 2 * kTileBytes /*Q*/ + kNumBuf * kTileBytes /*K,V*/ +
                            kIdRing * kMaxPagesPerChunk * 4 /*page ids*/ + 512 /*barriers*/ + 1024;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units: rescale O only when the max grows by > 2^8
+// mbarriers: q_full, buf_full/empty [kNumBuf], s_full [2], p_full [4], pv_done [2],
+// ids_full/empty [kIdRing], drain; then the TMEM slot and the abort flag
+static_assert((1 + 2 * kNumBuf + 2 + 4 + 2 + 2 * kIdRing + 1) * 8 + 8 <= 512, "barrier area");
+static_assert(kTileBytes % 1024 == 0 && (kIdRing * kMaxPagesPerChunk * 4) % 8 == 0, "buffer alignment");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 // Optional cycle stamps of CTA 0 (build with -DMTP_ATTN_TRACE): slot
 // (role, tile, iteration) -> clock64.  Compiled out otherwise.

@@ -44,6 +44,11 @@ constexpr int kMaxPages = 8;                     // page_size >= 8
 constexpr int kBarBytes = 640;                   // 64 mbarriers + TMEM slot + abort flag
 constexpr int kSmemBytes = 2 * kQTile + kNumBuf * kItem + kIdRing * kMaxPages * 4 + kBarBytes + 1024;
 constexpr float kRescaleThreshold = 8.0f;
+// mbarriers: q_full, buf_full/empty [kNumBuf], s_full [4], p_full [4], pv_done [2],
+// o_done [2], ids_full/empty [kIdRing], drain; then the TMEM slot and the abort flag
+static_assert((1 + 2 * kNumBuf + 4 + 4 + 2 + 2 + 2 * kIdRing + 1) * 8 + 8 <= kBarBytes, "barrier area");
+static_assert(kQTile % 1024 == 0 && kItem % 1024 == 0 && (kIdRing * kMaxPages * 4) % 8 == 0, "buffer alignment");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 template <int AB_FMT>
 __global__ void __launch_bounds__(kThreads, 1)

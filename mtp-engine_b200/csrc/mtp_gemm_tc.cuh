@@ -41,6 +41,15 @@ struct Cfg {
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;  // power of two >= 2*BN
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  // UMMA with M = 128: N a multiple of 16 in [16, 256]
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tile width");
+  // SW128 operand atoms are 8 rows x 128 bytes; every stage base stays 1024-byte aligned
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage alignment");
+  static_assert(STAGES >= 2, "at least a double-buffered ring");
+  // full/empty per stage, tfull/tempty x2, drain; then the TMEM slot and four flags (stream-K uses all)
+  static_assert((2 * STAGES + 5) * 8 + 5 * 4 <= BAR_BYTES, "barrier area");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+  static_assert(2 * BN <= TMEM_COLS && TMEM_COLS <= 512, "two accumulators in TMEM");
 };
 
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
