@@ -153,6 +153,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)  # before any workspace exists
+    N.set_gemm_tile_rows(1 if args.gemm_tile_rows == 256 else 0)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
@@ -422,7 +423,7 @@ def run_ours(args):
                    "seq_len": C5["S"],
                    "parallelism": "tp1" if world == 1 else f"tp{world} (cols / kv-heads / vocab)",
                    "l2": "inputs larger than L2 (about 2.3 GB touched per step)",
-                   "gemm_schedule": args.gemm_schedule,
+                   "gemm_schedule": args.gemm_schedule, "gemm_tile_rows": args.gemm_tile_rows,
                    "exchange": args.exchange if world > 1 else "none"},
         "roofline": roofline,
         "cpu_baseline": cpu,
@@ -554,6 +555,7 @@ def run_sweep(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
+    N.set_gemm_tile_rows(1 if args.gemm_tile_rows == 256 else 0)
     peaks = load_peaks()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     f32 = lambda t: t.detach().float().cpu().numpy()
@@ -583,7 +585,7 @@ def run_sweep(args):
 
     def emit(name, units, unit, t, bound, achieved, peak, peak_src, cpu_units, cpu_t, extra=None):
         line = {"sweep": True, "config": name, "metric": f"{unit} ({name})", "value": units / t, "unit": unit,
-                "gemm_schedule": args.gemm_schedule,
+                "gemm_schedule": args.gemm_schedule, "gemm_tile_rows": args.gemm_tile_rows,
                 "ms": t * 1e3, "dtype": extra.pop("dtype") if extra and "dtype" in extra else "bf16",
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak,
                              "unit": "TFLOP/s" if bound == "tensor" else "GB/s", "frac": achieved / peak,
@@ -597,15 +599,21 @@ def run_sweep(args):
     iters = max(5, min(args.steps, 50))
     # --compare: each GEMM config under both schedules, config 4 under both
     # attention kernels (one line per variant)
-    gemm_variants = ("dp", "streamk") if args.compare else (args.gemm_schedule,)
+    # GEMM variants: (label, schedule, tile-rows mode); "dp-256rows" = data-parallel 256 x 256 tiles
+    base_rows = 1 if args.gemm_tile_rows == 256 else 0
+    gemm_variants = ((("dp", 0, 0), ("streamk", 1, 0), ("dp-256rows", 0, 1)) if args.compare else
+                     ((args.gemm_schedule + ("-256rows" if base_rows else ""),
+                       1 if args.gemm_schedule == "streamk" else 0, base_rows),))
     attn_variants = (1, 2) if args.compare else (N.attn_kernel(),)
 
     def timed_gemm(fn):
         out = []
-        for v in gemm_variants:
-            N.set_gemm_schedule(1 if v == "streamk" else 0)
-            out.append((v, time_call(fn, iters)))
+        for label, sched, rows_mode in gemm_variants:
+            N.set_gemm_schedule(sched)
+            N.set_gemm_tile_rows(rows_mode)
+            out.append((label, time_call(fn, iters)))
         N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
+        N.set_gemm_tile_rows(base_rows)
         return out
 
     # ---- config 2 sweep: RMSNorm-linear bf16, gamma on
@@ -789,12 +797,15 @@ def run_profile_case(args):
     workload the ncu captures in profiles/ are taken on."""
     import torch
 
+    import _mtp_native as N
     import mtp_fused_verify as mv
     import mtp_kernels as mk
     from mtp_draft_tree import SpeculativeDraftTree
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
+    N.set_gemm_tile_rows(1 if args.gemm_tile_rows == 256 else 0)
     case = args.profile_case
     if case == "attention":
         B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
@@ -858,6 +869,9 @@ def main():
                          "kernels, the single-query lines under both decode kernels")
     ap.add_argument("--gemm-schedule", choices=["dp", "streamk"], default="dp",
                     help="tensor-core GEMM schedule: whole tiles per CTA, or stream-K where it is faster")
+    ap.add_argument("--gemm-tile-rows", type=int, choices=[128, 256], default=128,
+                    help="rows per data-parallel GEMM tile: 256 = 256 x 256 tiles (two MMAs share each weight "
+                         "stage) where a launch keeps two full rounds of them")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

@@ -62,6 +62,8 @@ SIGNATURES = {
     "mtp_verify_shard_keys_ws": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
+    "mtp_set_gemm_tile_rows": (_i, [_i]),
+    "mtp_gemm_tile_rows": (_i, []),
     "mtp_nccl_version": (_i, [ctypes.POINTER(_i)]),
     "mtp_nccl_unique_id": (_i, [_vp]),
     "mtp_nccl_comm_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i]),
@@ -117,6 +119,8 @@ def lib() -> ctypes.CDLL:
                     fn.argtypes = args
                 if os.environ.get("MTP_GEMM_STREAMK") == "1":  # before any workspace exists
                     L.mtp_set_gemm_schedule(1)
+                if os.environ.get("MTP_GEMM_ROWS") in ("0", "1", "2"):
+                    L.mtp_set_gemm_tile_rows(int(os.environ["MTP_GEMM_ROWS"]))
                 _lib = L
     return _lib
 
@@ -221,6 +225,17 @@ def _rest_fill(device: torch.device):
 
 def gemm_schedule() -> int:
     return int(lib().mtp_gemm_schedule())
+
+
+def gemm_tile_rows() -> int:
+    return int(lib().mtp_gemm_tile_rows())
+
+
+def set_gemm_tile_rows(mode: int) -> None:
+    """0 = 128-row GEMM tiles, 1 = 256 x 256 tiles where they pay, 2 = 256-row
+    tiles for every tensor-core GEMM with more than 128 rows (tests).  Needs
+    no workspace change: the tiles use the data-parallel schedule."""
+    check(lib().mtp_set_gemm_tile_rows(int(mode)), "mtp_set_gemm_tile_rows")
 
 
 def set_gemm_schedule(mode: int) -> None:

@@ -139,11 +139,11 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool fp8, int dt16, int6
 }
 
 // ---------------------------------------------------------------- GEMM launchers
-template <int BN, bool FP8, int FMT>
+template <int BN, bool FP8, int FMT, int MH = 1>
 int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int num_kb, const GemmEpilogue& ep,
                    cudaStream_t s) {
-  auto kern = tc::gemm_tc_kernel<BN, FP8, FMT>;
-  constexpr int smem = tc::Cfg<BN>::SMEM_BYTES;
+  auto kern = tc::gemm_tc_kernel<BN, FP8, FMT, MH>;
+  constexpr int smem = tc::Cfg<BN, MH>::SMEM_BYTES;
   int dev;
   if (int st = current_device(&dev)) return st;
   static bool attr_done[kMaxDevices] = {false};
@@ -151,7 +151,8 @@ int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
     MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_done[dev] = true;
   }
-  const int tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + BN - 1) / BN);
+  constexpr int tile_m = tc::Cfg<BN, MH>::TILE_M;
+  const int tiles = ((M + tile_m - 1) / tile_m) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   kern<<<grid, tc::kThreads, smem, s>>>(ta, tb, M, N, num_kb, ep);
   MTP_LAUNCH_CHECK();
@@ -190,6 +191,25 @@ int launch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, in
     case 128: return launch_tc_inst<128, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
     default: return launch_tc_inst<64, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
   }
+}
+
+// Process-wide row height of the data-parallel tiles (mtp_set_gemm_tile_rows):
+// 0 = 128-row tiles (default); 1 = 256-row tiles x 256 columns where
+// use_tall_tiles() expects them to pay; 2 = 256-row tiles for every
+// tensor-core GEMM with more than 128 rows (tests).
+std::atomic<int> g_gemm_rows{0};
+
+// 256 x 256 tiles read (256 + 256) operand rows per K block for twice the
+// MMA work of a 128 x 256 tile's (128 + 256): a third less operand traffic
+// per FLOP.  Their two accumulators fill TMEM (no double buffering, so each
+// tile's epilogue is exposed), and they halve the tile count, so they are
+// used only where a launch still has at least two full rounds of tiles.
+bool use_tall_tiles(int64_t M, int64_t N, int sms) {
+  const int mode = g_gemm_rows.load(std::memory_order_relaxed);
+  if (mode == 0 || M <= tc::kBM) return false;
+  if (mode == 2) return true;
+  const int64_t tiles = ((M + 2 * tc::kBM - 1) / (2 * tc::kBM)) * ((N + 255) / 256);
+  return tiles >= 2 * (int64_t)sms;
 }
 
 // ---------------------------------------------------------------- stream-K
@@ -349,12 +369,19 @@ int launch_gemm_tc(const void* A, const void* B, int ab_dtype, bool fp8, int64_t
   }
   int dev;
   if (int st = current_device(&dev)) return st;
-  const int bn = pick_bn(M, N, sm_count(dev));
+  const bool tall = use_tall_tiles(M, N, sm_count(dev));
+  const int bn = tall ? 256 : pick_bn(M, N, sm_count(dev));
   CUtensorMap ta, tb;
+  // the A box stays 128 rows: a tall tile loads its two row halves separately
   if (int st = make_kmajor_map(&ta, A, fp8, ab_dtype, M, K, tc::kBM)) return st;
   if (int st = make_kmajor_map(&tb, B, fp8, ab_dtype, N, K, bn)) return st;
   const int eb = fp8 ? 1 : 2;
   const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  if (tall) {
+    if (fp8) return launch_tc_inst<256, true, 0, 2>(ta, tb, (int)M, (int)N, num_kb, ep, s);
+    if (ab_dtype == MTP_DTYPE_BF16) return launch_tc_inst<256, false, 1, 2>(ta, tb, (int)M, (int)N, num_kb, ep, s);
+    return launch_tc_inst<256, false, 0, 2>(ta, tb, (int)M, (int)N, num_kb, ep, s);
+  }
   if (fp8) return launch_tc_bn<true, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
   if (ab_dtype == MTP_DTYPE_BF16) return launch_tc_bn<false, 1>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
   return launch_tc_bn<false, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
@@ -548,6 +575,14 @@ int mtp_set_gemm_schedule(int mode) {
 }
 
 int mtp_gemm_schedule(void) { return g_gemm_schedule.load(std::memory_order_relaxed); }
+
+int mtp_set_gemm_tile_rows(int mode) {
+  if (mode < 0 || mode > 2) return fail(MTP_ERR_ARG, "GEMM tile-rows mode %d (expected 0, 1 or 2)", mode);
+  g_gemm_rows.store(mode, std::memory_order_relaxed);
+  return MTP_OK;
+}
+
+int mtp_gemm_tile_rows(void) { return g_gemm_rows.load(std::memory_order_relaxed); }
 
 size_t mtp_gemm_streamk_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype) {
   if (M <= 0 || N <= 0 || K <= 0 || !valid_dtype(ab_dtype) || ab_dtype == MTP_DTYPE_F32) return 0;

@@ -32,34 +32,56 @@ constexpr int kBM = 128;
 constexpr int kThreads = 192;
 constexpr int kKBlockBytes = 128;  // one 128-byte swizzle row of K per stage
 
-template <int BN>
+// MH = row halves per tile: 1 -> 128 x BN tiles; 2 -> 256 x BN tiles, two
+// M=128 MMAs per K step sharing one B (weight) stage, which cuts the operand
+// traffic per FLOP from (128 + BN) / (128 BN) to (256 + BN) / (256 BN) rows.
+template <int BN, int MH = 1>
 struct Cfg {
-  static constexpr int A_BYTES = kBM * kKBlockBytes;
+  static constexpr int TILE_M = MH * kBM;
+  static constexpr int HALF_BYTES = kBM * kKBlockBytes;  // one 128-row half of an A stage
+  static constexpr int A_BYTES = MH * HALF_BYTES;
   static constexpr int B_BYTES = BN * kKBlockBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (220 * 1024 / STAGE_BYTES) < 8 ? (220 * 1024 / STAGE_BYTES) : 8;
-  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;  // power of two >= 2*BN
+  static constexpr int ACC_COLS = MH * BN;                        // one tile's accumulators
+  static constexpr int ACC_BUFS = (2 * ACC_COLS <= 512) ? 2 : 1;  // double-buffered when two fit
+  static constexpr int TMEM_COLS = (ACC_BUFS * ACC_COLS <= 256) ? 256 : 512;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(MH == 1 || MH == 2, "one or two row halves");
   // UMMA with M = 128: N a multiple of 16 in [16, 256]
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tile width");
   // SW128 operand atoms are 8 rows x 128 bytes; every stage base stays 1024-byte aligned
-  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage alignment");
+  static_assert(HALF_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage alignment");
   static_assert(STAGES >= 2, "at least a double-buffered ring");
   // full/empty per stage, tfull/tempty x2, drain; then the TMEM slot and four flags (stream-K uses all)
   static_assert((2 * STAGES + 5) * 8 + 5 * 4 <= BAR_BYTES, "barrier area");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
-  static_assert(2 * BN <= TMEM_COLS && TMEM_COLS <= 512, "two accumulators in TMEM");
+  static_assert(ACC_BUFS * ACC_COLS <= TMEM_COLS && TMEM_COLS <= 512, "accumulators in TMEM");
 };
+
+// Tile t, taken by a CTA in round j (t = blockIdx.x + j * gridDim.x) -> row
+// tile mb and column tile nb, M-fastest so the CTAs that share a weight tile
+// run at the same time.  With 256-row tiles the last row tile is often half
+// empty (384 verify rows = 256 + 128); when the grid is a multiple of num_m
+// the plain order would give each CTA the same row tile in every round, so
+// the row tile is rotated by the round instead -- still a permutation of the
+// tiles of each round, and every CTA sees every row tile in turn.
+template <int MH>
+__device__ __forceinline__ void tile_coords(int t, int j, int num_m, int& mb, int& nb) {
+  nb = t / num_m;
+  if (MH == 2 && gridDim.x % num_m == 0) mb = (t + j) % num_m;
+  else mb = t % num_m;
+}
 
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // ab_fmt: 0 = f16, 1 = bf16 (kind::f16); FP8: E4M3 x E4M3 (kind::f8f6f4)
-template <int BN, bool FP8, int AB_FMT>
+template <int BN, bool FP8, int AB_FMT, int MH = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                    int N, int num_kb, GemmEpilogue ep) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MH>;
   constexpr int KB_ELEMS = FP8 ? 128 : 64;       // elements per 128-byte K block
   constexpr int UMMA_K_BYTES = 32;               // K per tcgen05.mma: 16 x 16-bit or 32 x 8-bit
   constexpr int K_STEPS = kKBlockBytes / UMMA_K_BYTES;
@@ -109,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_m = (M + kBM - 1) / kBM;
+  const int num_m = (M + C::TILE_M - 1) / C::TILE_M;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
 
@@ -119,15 +141,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int mb = t % num_m, nb = t / num_m;
+      for (int t = blockIdx.x, j = 0; t < num_tiles && ok; t += gridDim.x, ++j) {
+        int mb, nb;
+        tile_coords<MH>(t, j, num_m, mb, nb);
+        // a row half that lies wholly past M is neither loaded nor multiplied
+        const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, kb * KB_ELEMS, mb * kBM, &full[stage]);
+          mbar_expect_tx(&full[stage], halves * C::HALF_BYTES + C::B_BYTES);
+          for (int h = 0; h < halves; ++h)
+            tma_load_2d(sA + stage * C::A_BYTES + h * C::HALF_BYTES, &tmA, kb * KB_ELEMS, mb * C::TILE_M + h * kBM,
+                        &full[stage]);
           tma_load_2d(sB + stage * C::B_BYTES, &tmB, kb * KB_ELEMS, nb * BN, &full[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -144,14 +171,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int local = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        int mb, nb;
+        tile_coords<MH>(t, local, num_m, mb, nb);
+        const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
+        const int acc = C::ACC_BUFS == 2 ? (local & 1) : 0;
+        const uint32_t acc_phase = C::ACC_BUFS == 2 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * C::ACC_COLS);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
@@ -162,10 +192,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < K_STEPS; ++k) {
-            const uint64_t ad = sw128_kmajor_desc(a_addr + k * UMMA_K_BYTES);
             const uint64_t bd = sw128_kmajor_desc(b_addr + k * UMMA_K_BYTES);
-            if constexpr (FP8) umma_f8(d_tmem, ad, bd, IDESC, (kb | k) != 0);
-            else umma_f16(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) {
+              if (h >= halves) break;
+              // half h: rows h*128.. of the tile, accumulator columns h*BN..
+              const uint64_t ad = sw128_kmajor_desc(a_addr + h * C::HALF_BYTES + k * UMMA_K_BYTES);
+              if constexpr (FP8) umma_f8(d_tmem + (uint32_t)(h * BN), ad, bd, IDESC, (kb | k) != 0);
+              else umma_f16(d_tmem + (uint32_t)(h * BN), ad, bd, IDESC, (kb | k) != 0);
+            }
           }
           umma_commit(&empty[stage]);  // frees this stage once its MMAs have read it
           if (++stage == C::STAGES) {
@@ -186,81 +221,87 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = q * 32 + lane;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
-      const int mb = t % num_m, nb = t / num_m;
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      int mb, nb;
+      tile_coords<MH>(t, local, num_m, mb, nb);
+      const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
+      const int acc = C::ACC_BUFS == 2 ? (local & 1) : 0;
+      const uint32_t acc_phase = C::ACC_BUFS == 2 ? ((local >> 1) & 1) : (local & 1);
       const bool got = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      const int row = mb * kBM + row_in_tile;
-      const bool row_ok = row < M;
-      const uint32_t tbase = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
-      if (ep.mode == EPI_STORE) {
-        const float rs = (ep.row_scale && row_ok) ? ep.row_scale[row] : 1.0f;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_wait_ld();
-          const int n0 = nb * BN + c * 32;
-          if (!row_ok || n0 >= N) continue;
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            float x = __uint_as_float(r[j]) * rs;
-            if (n < N) {
-              if (ep.col_scale) x *= ep.col_scale[n];
-              if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
+      for (int h = 0; h < halves; ++h) {
+        const int row = mb * C::TILE_M + h * kBM + row_in_tile;
+        const bool row_ok = row < M;
+        const uint32_t tbase =
+            tmem_base + (uint32_t)(acc * C::ACC_COLS + h * BN) + ((uint32_t)(q * 32) << 16);
+        if (ep.mode == EPI_STORE) {
+          const float rs = (ep.row_scale && row_ok) ? ep.row_scale[row] : 1.0f;
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_wait_ld();
+            const int n0 = nb * BN + c * 32;
+            if (!row_ok || n0 >= N) continue;
+            float v[32];
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + j;
+              float x = __uint_as_float(r[j]) * rs;
+              if (n < N) {
+                if (ep.col_scale) x *= ep.col_scale[n];
+                if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
+              }
+              v[j] = x * ep.scale;
             }
-            v[j] = x * ep.scale;
+            const int64_t off = (int64_t)row * ep.ldy + n0;
+            if (ep.y_vec_ok && n0 + 32 <= N && ep.y_dtype != MTP_DTYPE_F32) {
+              uint32_t packed[16];
+  #pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (ep.y_dtype == MTP_DTYPE_BF16) {
+                  __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                  packed[j] = *reinterpret_cast<uint32_t*>(&h);
+                } else {
+                  __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                  packed[j] = *reinterpret_cast<uint32_t*>(&h);
+                }
+              }
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.y) + off);
+  #pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+            } else {
+              for (int j = 0; j < 32 && n0 + j < N; ++j) store_f32(ep.y, ep.y_dtype, off + j, v[j]);
+            }
           }
-          const int64_t off = (int64_t)row * ep.ldy + n0;
-          if (ep.y_vec_ok && n0 + 32 <= N && ep.y_dtype != MTP_DTYPE_F32) {
-            uint32_t packed[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (ep.y_dtype == MTP_DTYPE_BF16) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-                packed[j] = *reinterpret_cast<uint32_t*>(&h);
-              } else {
-                __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-                packed[j] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          int32_t best = INT32_MIN;
+          int best_n = nb * BN;
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_wait_ld();
+            const int n0 = nb * BN + c * 32;
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + j;
+              if (n < N) {
+                float x = __uint_as_float(r[j]);
+                if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
+                const int32_t o = ordered_i32(x);
+                if (o > best) {  // strict: the first (lowest) index wins a tie
+                  best = o;
+                  best_n = n;
+                }
               }
             }
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.y) + off);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32 && n0 + j < N; ++j) store_f32(ep.y, ep.y_dtype, off + j, v[j]);
           }
+          if (row_ok) atomicMax(&ep.keys[row], make_key(best, (uint32_t)(ep.col_offset + best_n)));
         }
-      } else {
-        int32_t best = INT32_MIN;
-        int best_n = nb * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_wait_ld();
-          const int n0 = nb * BN + c * 32;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            if (n < N) {
-              float x = __uint_as_float(r[j]);
-              if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
-              const int32_t o = ordered_i32(x);
-              if (o > best) {  // strict: the first (lowest) index wins a tie
-                best = o;
-                best_n = n;
-              }
-            }
-          }
-        }
-        if (row_ok) atomicMax(&ep.keys[row], make_key(best, (uint32_t)(ep.col_offset + best_n)));
-      }
+      }  // row halves
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }

@@ -20,6 +20,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 # name -> (test files, extra environment, -k expression)
 CHILDREN = {
     "streamk": (["test_gpu_streamk.py"], {}, None),
+    "tall_tiles": (["test_gpu_tall_tiles.py"], {}, None),
     "tree_attn_rmsnorm_linear": (["test_gpu_tree_attn_rmsnorm_linear.py"], {}, None),
     "nccl_abi": (["test_gpu_nccl_abi.py"], {"NCCL_NVLS_ENABLE": "0"}, None),
     "attention_64key_kernel": (["test_gpu_attention_tc.py", "test_gpu_parity.py"], {"MTP_ATTN_KERNEL": "2"},

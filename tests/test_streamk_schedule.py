@@ -111,3 +111,17 @@ def test_whole_tile_plan_covers_every_block_once(M, Nn, K, dt):
     when stream-K does not pay: a ragged last round must be skipped, not
     run past the last tile."""
     check(M, Nn, K, dt, grid=-1)
+
+
+def test_tile_rows_switch_roundtrip():
+    """The 256-row tile switch (no device needed to set it)."""
+    L = N.lib()
+    before = L.mtp_gemm_tile_rows()
+    assert before in (0, 1, 2)
+    try:
+        for m in (0, 1, 2):
+            N.set_gemm_tile_rows(m)
+            assert L.mtp_gemm_tile_rows() == m == N.gemm_tile_rows()
+        assert L.mtp_set_gemm_tile_rows(-1) == 8 and L.mtp_set_gemm_tile_rows(3) == 8  # MTP_ERR_ARG
+    finally:
+        N.set_gemm_tile_rows(before)
