@@ -871,7 +871,7 @@ def main():
                     help="tensor-core GEMM schedule: whole tiles per CTA, or stream-K where it is faster")
     ap.add_argument("--gemm-tile-rows", type=int, choices=[128, 256], default=128,
                     help="rows per data-parallel GEMM tile: 256 = 256 x 256 tiles (two MMAs share each weight "
-                         "stage) where a launch keeps two full rounds of them")
+                         "stage) where the cost model expects them to be faster")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

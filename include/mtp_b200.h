@@ -79,14 +79,19 @@ int mtp_gemm_schedule(void);
 /* Process-wide row height of the tensor-core GEMM's data-parallel tiles
  * (mtp_rmsnorm_linear, its FP8 variant, the verify GEMMs): 0 (default) =
  * 128-row tiles; 1 = 256 x 256 tiles, two M=128 MMAs per K step sharing the
- * weight stage (a third less operand traffic per FLOP), where a launch still
- * has two full rounds of such tiles; 2 = 256-row tiles for every such GEMM
- * with more than 128 rows (for tests).  Results are bit-identical across
+ * weight stage (a third less operand traffic per FLOP), where a cost model
+ * (rounds x max(MMA, operand traffic) per K block) expects them to be faster;
+ * 2 = 256-row tiles for every such GEMM with more than 128 rows (for tests).  Results are bit-identical across
  * modes.  The environment variable MTP_GEMM_ROWS (0/1/2) sets the initial
  * value when the Python package loads the library.  Returns MTP_ERR_ARG for
  * other values. */
 int mtp_set_gemm_tile_rows(int mode);
 int mtp_gemm_tile_rows(void);
+
+/* Test support, host only: the tile (*rows x *bn) that the data-parallel
+ * tensor-core GEMM of C[M,N] would use on `sms` SMs under the current
+ * tile-rows mode. */
+int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* rows, int* bn);
 
 /* Process-wide choice of the paged tree-attention kernel behind
  * mtp_tree_attention_paged: 1 (default) = 128-key chunks; 2 = 64-key chunks

@@ -64,6 +64,7 @@ SIGNATURES = {
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
     "mtp_set_gemm_tile_rows": (_i, [_i]),
     "mtp_gemm_tile_rows": (_i, []),
+    "mtp_gemm_tile_plan": (_i, [_i64, _i64, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "mtp_nccl_version": (_i, [ctypes.POINTER(_i)]),
     "mtp_nccl_unique_id": (_i, [_vp]),
     "mtp_nccl_comm_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i]),
@@ -232,7 +233,8 @@ def gemm_tile_rows() -> int:
 
 
 def set_gemm_tile_rows(mode: int) -> None:
-    """0 = 128-row GEMM tiles, 1 = 256 x 256 tiles where they pay, 2 = 256-row
+    """0 = 128-row GEMM tiles, 1 = 256 x 256 tiles where the cost model
+    expects them to be faster, 2 = 256-row
     tiles for every tensor-core GEMM with more than 128 rows (tests).  Needs
     no workspace change: the tiles use the data-parallel schedule."""
     check(lib().mtp_set_gemm_tile_rows(int(mode)), "mtp_set_gemm_tile_rows")

@@ -199,17 +199,31 @@ int launch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, in
 // tensor-core GEMM with more than 128 rows (tests).
 std::atomic<int> g_gemm_rows{0};
 
+// Cycles per K block of one tile of R rows x BN columns: the larger of the
+// MMA time (R x BN x 64 MACs at 8192 FLOP per clock per SM) and the time to
+// move its (R + BN) operand rows of 128 bytes into shared memory at an
+// assumed ~64 B per clock per SM from L2.
+inline int64_t kblock_cycles(int64_t R, int64_t BN) {
+  const int64_t mma = R * BN / 64, traffic = 2 * (R + BN);
+  return mma > traffic ? mma : traffic;
+}
+
 // 256 x 256 tiles read (256 + 256) operand rows per K block for twice the
 // MMA work of a 128 x 256 tile's (128 + 256): a third less operand traffic
 // per FLOP.  Their two accumulators fill TMEM (no double buffering, so each
-// tile's epilogue is exposed), and they halve the tile count, so they are
-// used only where a launch still has at least two full rounds of tiles.
+// tile's epilogue is exposed, counted as 3 %), and they halve the tile
+// count.  Mode 1 takes them where rounds x cycles per K block come out
+// lower than for the 128-row tiles pick_bn would choose.
 bool use_tall_tiles(int64_t M, int64_t N, int sms) {
   const int mode = g_gemm_rows.load(std::memory_order_relaxed);
   if (mode == 0 || M <= tc::kBM) return false;
   if (mode == 2) return true;
-  const int64_t tiles = ((M + 2 * tc::kBM - 1) / (2 * tc::kBM)) * ((N + 255) / 256);
-  return tiles >= 2 * (int64_t)sms;
+  const int bn = pick_bn(M, N, sms);
+  const int64_t tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + bn - 1) / bn);
+  const int64_t cost = (tiles + sms - 1) / sms * kblock_cycles(tc::kBM, bn);
+  const int64_t tall_tiles = ((M + 2 * tc::kBM - 1) / (2 * tc::kBM)) * ((N + 255) / 256);
+  const int64_t tall_cost = (tall_tiles + sms - 1) / sms * kblock_cycles(2 * tc::kBM, 256) * 103 / 100;
+  return tall_cost < cost;
 }
 
 // ---------------------------------------------------------------- stream-K
@@ -583,6 +597,14 @@ int mtp_set_gemm_tile_rows(int mode) {
 }
 
 int mtp_gemm_tile_rows(void) { return g_gemm_rows.load(std::memory_order_relaxed); }
+
+int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* rows, int* bn) {
+  if (M <= 0 || N <= 0 || sms <= 0 || !rows || !bn) return fail(MTP_ERR_ARG, "bad tile-plan arguments");
+  const bool tall = use_tall_tiles(M, N, sms);
+  *rows = tall ? 2 * tc::kBM : tc::kBM;
+  *bn = tall ? 256 : pick_bn(M, N, sms);
+  return MTP_OK;
+}
 
 size_t mtp_gemm_streamk_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype) {
   if (M <= 0 || N <= 0 || K <= 0 || !valid_dtype(ab_dtype) || ab_dtype == MTP_DTYPE_F32) return 0;

@@ -125,3 +125,28 @@ def test_tile_rows_switch_roundtrip():
         assert L.mtp_set_gemm_tile_rows(-1) == 8 and L.mtp_set_gemm_tile_rows(3) == 8  # MTP_ERR_ARG
     finally:
         N.set_gemm_tile_rows(before)
+
+
+def tile_plan(M, Nn, sms=SMS):
+    rows, bn = ctypes.c_int(0), ctypes.c_int(0)
+    N.check(N.lib().mtp_gemm_tile_plan(M, Nn, sms, ctypes.byref(rows), ctypes.byref(bn)), "mtp_gemm_tile_plan")
+    return rows.value, bn.value
+
+
+def test_tile_plan_choices():
+    """Which workloads the cost model sends to 256 x 256 tiles (mode 1)."""
+    before = N.gemm_tile_rows()
+    try:
+        N.set_gemm_tile_rows(0)
+        assert tile_plan(384, 128256) == (128, 256) and tile_plan(512, 14336)[0] == 128
+        N.set_gemm_tile_rows(1)
+        assert tile_plan(384, 128256) == (256, 256)   # config 5, 1 GPU: 7 rounds instead of 11
+        assert tile_plan(384, 16032) == (256, 256)    # config 5, 1 of 8 ranks: 1 round instead of 2
+        assert tile_plan(512, 14336) == (256, 256)    # config 2, 1 GPU: 112 tiles in one round
+        assert tile_plan(512, 1792)[0] == 128         # config 2, 1 of 8 ranks: 28 tiles fit one round
+        assert tile_plan(64, 128256)[0] == 128        # one row half only
+        assert tile_plan(128, 100000)[0] == 128
+        N.set_gemm_tile_rows(2)
+        assert tile_plan(129, 64) == (256, 256) and tile_plan(128, 64)[0] == 128
+    finally:
+        N.set_gemm_tile_rows(before)
