@@ -159,6 +159,12 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     prim = mp.get_parallel_primitives()
     assert C2["N"] % world == 0 and C4["Hkv"] % world == 0
+    # strong: the 1-GPU job split tensor-parallel (columns / KV heads / vocabulary).
+    # weak: configs 2 and 4 run whole on every GPU over that rank's own batch; the
+    # verify checks every rank's candidates against a vocabulary-sharded lm_head
+    # (the candidates all-gathered, the argmax keys all-reduced).
+    weak = world > 1 and args.scaling == "weak"
+    split = 1 if weak else world
     comm = None  # --exchange abi: the library's own NCCL communicator (C ABI)
     if world > 1 and args.exchange == "abi":
         uid = [mp.NcclCommunicator.unique_id() if rank == 0 else None]
@@ -167,12 +173,12 @@ def run_ours(args):
 
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     # ---- stage 1 inputs (columns split)
-    Nr = C2["N"] // world
+    Nr = C2["N"] // split
     x = torch.randn(C2["M"], C2["K"], generator=g, device=dev).to(torch.bfloat16)
     gamma = 1.0 + 0.1 * torch.randn(C2["K"], generator=g, device=dev)
     W = (0.02 * torch.randn(Nr, C2["K"], generator=g, device=dev)).to(torch.bfloat16)
     # ---- stage 2 inputs (KV heads split)
-    Hkv = C4["Hkv"] // world
+    Hkv = C4["Hkv"] // split
     Hq = Hkv * (C4["Hq"] // C4["Hkv"])
     B4, D, ps, ctx, P = C4["B"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
     kp = torch.randn(P, B4, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
@@ -191,25 +197,39 @@ def run_ours(args):
     # ---- stage 3 inputs (vocabulary split)
     B5, S5, K5, V5 = C5["B"], C5["S"], C5["K"], C5["V"]
     lo, hi = mp.vocab_shard_range(V5, world, rank)
-    gh = torch.Generator(device=dev).manual_seed(4)  # hidden states identical on every rank
-    hidden = torch.randn(B5, S5, K5, generator=gh, device=dev).to(torch.bfloat16)
+    BG = B5 * (world if weak else 1)  # sequences verified per step, all ranks
+    gh = torch.Generator(device=dev).manual_seed(4)  # identical on every rank; weak: rank r owns block r
+    hidden_g = torch.randn(BG, S5, K5, generator=gh, device=dev).to(torch.bfloat16)
     lm = (0.02 * torch.randn(hi - lo, K5, generator=g, device=dev)).to(torch.bfloat16)
     # drafts with per-sequence accept prefixes U{0..5}: needs the true argmax
-    keys = torch.full((B5 * S5,), -(2 ** 63), dtype=torch.int64, device=dev)
-    N.check(N.lib().mtp_verify_shard_keys(N.ptr(hidden), N.DT_BF16, N.ptr(lm), N.DT_BF16, None, 0, N.ptr(keys),
-                                          B5 * S5, K5, hi - lo, lo, N.stream_handle(dev)), "setup keys")
+    keys = torch.full((BG * S5,), -(2 ** 63), dtype=torch.int64, device=dev)
+    N.check(N.lib().mtp_verify_shard_keys(N.ptr(hidden_g), N.DT_BF16, N.ptr(lm), N.DT_BF16, None, 0, N.ptr(keys),
+                                          BG * S5, K5, hi - lo, lo, N.stream_handle(dev)), "setup keys")
     if world > 1:
         dist.all_reduce(keys, op=dist.ReduceOp.MAX)
-    top = mp.key_index(keys).cpu().numpy().reshape(B5, S5)
+    top = mp.key_index(keys).cpu().numpy().reshape(BG, S5)
     rng = np.random.default_rng(4)
-    draft_np = rng.integers(0, V5, size=(B5, S5 - 1))
-    for b in range(B5):
+    draft_np = rng.integers(0, V5, size=(BG, S5 - 1))
+    for b in range(BG):
         a = int(rng.integers(0, S5))
         draft_np[b, :a] = top[b, 1:a + 1]
         if a < S5 - 1:
             while draft_np[b, a] == top[b, a + 1]:
                 draft_np[b, a] = rng.integers(0, V5)
-    draft = torch.tensor(draft_np, dtype=torch.int32, device=dev)
+    own = slice(rank * B5, (rank + 1) * B5) if weak else slice(0, B5)
+    hidden = hidden_g[own].contiguous()
+    draft = torch.tensor(draft_np[own], dtype=torch.int32, device=dev)
+    del hidden_g
+    # weak: every rank's candidates gathered here before the verify
+    hid_all = torch.empty((BG, S5, K5), dtype=torch.bfloat16, device=dev) if weak else None
+    dr_all = torch.empty((BG, S5 - 1), dtype=torch.int32, device=dev) if weak else None
+    pending = []  # weak: an all-gather issued early in the step, awaited by the verify
+
+    def gather(hh, dd):
+        """Start the all-gather of this rank's candidates (async; it overlaps
+        whatever the stream runs next)."""
+        pending.append((dist.all_gather_into_tensor(hid_all, hh, async_op=True),
+                        dist.all_gather_into_tensor(dr_all, dd, async_op=True)))
 
     def stage1(xx):
         return mk.fused_rmsnorm_linear(xx, W, None, C2["eps"], norm_weight=gamma)
@@ -220,6 +240,12 @@ def run_ours(args):
     def stage3(hh, dd):
         if world == 1:
             return mv.fused_multi_verify(hh, lm, dd)
+        if weak:
+            if not pending:
+                gather(hh, dd)
+            for w_ in pending.pop():
+                w_.wait()  # the stream waits for the gather, the host does not
+            hh, dd = hid_all, dr_all
         if comm is not None:
             return mp.vocab_parallel_multi_verify_nccl(hh, lm, dd, lo, comm)
         return mp.vocab_parallel_multi_verify(hh, lm, dd, None, lo, prim, exchange=args.exchange)
@@ -247,7 +273,7 @@ def run_ours(args):
     # 2-8 GPUs the replays saved only a few percent.
     # With the peer-memory exchange the verify holds no NCCL call, so its graph
     # needs no special teardown: replay graphs on N > 1 too.
-    use_graphs = (world == 1 or args.graph or args.exchange in ("p2p", "fused")) and not args.no_graph
+    use_graphs = (world == 1 or args.graph or args.exchange in ("p2p", "fused")) and not args.no_graph and not weak
     launches0 = N.lib().mtp_launch_count()
     graphs = []  # the only owner of the graph objects
     if use_graphs:
@@ -278,6 +304,8 @@ def run_ours(args):
         for i in range(args.steps):
             e = ev[i]
             e[0].record(stream)
+            if weak:
+                gather(hidden, draft)  # overlaps stages 1 and 2
             run[0]()
             e[1].record(stream)
             run[1]()
@@ -297,7 +325,8 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, s1, s2, s3 = t.tolist()
     ms_per_step = total_ms / args.steps
-    value = TOKENS_PER_STEP * args.steps / (total_ms / 1e3)
+    tokens_per_step = TOKENS_PER_STEP * (world if weak else 1)
+    value = tokens_per_step * args.steps / (total_ms / 1e3)
 
     # ---- end to end through the public API, host buffers in and out
     pin = lambda tt: tt.cpu().pin_memory()
@@ -337,6 +366,8 @@ def run_ours(args):
                 out = run[j]()
                 if j == 2:
                     a, n_, c = graphs[2].outputs if graphs else out
+                    if weak:  # this rank reads back its own sequences
+                        a, n_, c = a[own], n_[own], c[own]
                     verified.record(stream)
                     d2h_stream.wait_event(verified)
                     with torch.cuda.stream(d2h_stream):
@@ -360,7 +391,7 @@ def run_ours(args):
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = TOKENS_PER_STEP * args.steps / (te.item() / 1e3)
+    e2e_value = tokens_per_step * args.steps / (te.item() / 1e3)
 
     status = N.device_status(dev)
     # graphs that hold NCCL calls must be gone before destroy_process_group:
@@ -381,8 +412,10 @@ def run_ours(args):
         return
 
     peaks = load_peaks()
-    # per-GPU rooflines: each rank does 1/world of every stage's work
-    w = float(world)
+    # per-GPU rooflines: strong -- each rank does 1/world of every stage's work;
+    # weak -- every rank does a whole config 2 and 4, and 1/world of a verify
+    # over world x 64 sequences (the FLOPs of one config-5 verify)
+    w = float(split)
     kernels = {
         "rmsnorm_linear": {"ms": s1, "bound": "tensor", "achieved": C2_FLOP / w / (s1 / 1e3) / 1e12,
                            "unit": "TFLOP/s", "flop_per_gpu": C2_FLOP / w, "bytes_per_gpu": C2_BYTES / w},
@@ -390,7 +423,8 @@ def run_ours(args):
                                  "unit": "GB/s", "bytes_per_gpu": C4_BYTES / w, "flop_per_gpu": C4_FLOP / w},
         "fused_multi_verify": {"ms": s3, "bound": "tensor", "achieved": C5_FLOP / w / (s3 / 1e3) / 1e12,
                                "unit": "TFLOP/s", "flop_per_gpu": C5_FLOP / w, "bytes_per_gpu": C5_BYTES / w,
-                               "note": "includes the NCCL key all-reduce when n_gpus > 1"},
+                               "note": "includes the NCCL key all-reduce when n_gpus > 1" +
+                                       (", and the wait for the candidates' all-gather" if weak else "")},
     }
     for k in kernels.values():
         if k["bound"] == "hbm":
@@ -417,11 +451,13 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) activations / KV, random-init weights of the BASELINE shapes",
-        "config": {"workload": WORKLOAD, "tokens_per_step": TOKENS_PER_STEP, "global_batch": C5["B"],
+        "config": {"workload": WORKLOAD, "tokens_per_step": tokens_per_step, "global_batch": BG,
                    "seq_len": C5["S"],
-                   "parallelism": "tp1" if world == 1 else f"tp{world} (cols / kv-heads / vocab)",
+                   "parallelism": "tp1" if world == 1 else
+                   (f"dp{world} (configs 2, 4 per GPU) + verify of {world}x{B5} sequences, vocab-sharded"
+                    if weak else f"tp{world} (cols / kv-heads / vocab)"),
                    "l2": "inputs larger than L2 (about 2.3 GB touched per step)",
                    "gemm_schedule": args.gemm_schedule, "gemm_tile_rows": args.gemm_tile_rows,
                    "exchange": args.exchange if world > 1 else "none"},
@@ -861,6 +897,9 @@ def main():
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
                          "the all-reduce fused into the shard GEMM, or the one-call C-ABI verify over the "
                          "library's own NCCL communicator")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="N > 1: strong = the 1-GPU job split tensor-parallel; weak = configs 2 and 4 whole on "
+                         "every GPU, the verify over every rank's sequences with the lm_head vocab-sharded")
     ap.add_argument("--profile-case", choices=["verify", "rms", "attention"], default=None,
                     help="call one operator at its BASELINE config --steps times (the workload of the ncu "
                          "captures in profiles/)")
