@@ -363,39 +363,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
-          chunk_values(c, v);
+          chunk_values(c, v);  // every warp loads: tcgen05.ld is warp-wide
           const int n0 = nb * BN + c * 32;
-          if (!row_ok || n0 >= N) continue;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            float x = v[j] * rs;
-            if (n < N) {
-              if (ep.col_scale) x *= ep.col_scale[n];
-              if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
-            }
-            v[j] = x * ep.scale;
-          }
-          const int64_t off = (int64_t)row * ep.ldy + n0;
-          if (ep.y_vec_ok && n0 + 32 <= N && ep.y_dtype != MTP_DTYPE_F32) {
-            uint32_t packed[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (ep.y_dtype == MTP_DTYPE_BF16) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-                packed[j] = *reinterpret_cast<uint32_t*>(&h);
-              } else {
-                __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-                packed[j] = *reinterpret_cast<uint32_t*>(&h);
-              }
-            }
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.y) + off);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32 && n0 + j < N; ++j) store_f32(ep.y, ep.y_dtype, off + j, v[j]);
-          }
+          if (row_ok && n0 < N) tc::epi_store32(ep, v, row, n0, N, rs);
         }
       } else {
         int32_t best = INT32_MIN;
@@ -404,20 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           chunk_values(c, v);
-          const int n0 = nb * BN + c * 32;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            if (n < N) {
-              float x = v[j];
-              if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
-              const int32_t o = ordered_i32(x);
-              if (o > best) {  // strict: the first (lowest) index wins a tie
-                best = o;
-                best_n = n;
-              }
-            }
-          }
+          tc::epi_argmax32(ep, v, nb * BN + c * 32, N, best, best_n);
         }
         if (row_ok) {
           const long long key = make_key(best, (uint32_t)(ep.col_offset + best_n));

@@ -76,6 +76,73 @@ __device__ __forceinline__ void tile_coords(int t, int j, int num_m, int& mb, in
 
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Store epilogue for 32 accumulator values of one row (row < M), columns
+// n0..n0+31 (n0 < N): y = (acc * rs * col_scale[n] + bias[n]) * scale in y's
+// dtype, as 16-byte stores when the 32 columns are all inside N and aligned.
+__device__ __forceinline__ void epi_store32(const GemmEpilogue& ep, const float (&acc)[32], int64_t row, int n0,
+                                            int N, float rs) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int n = n0 + j;
+    float x = acc[j] * rs;
+    if (n < N) {
+      if (ep.col_scale) x *= ep.col_scale[n];
+      if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
+    }
+    v[j] = x * ep.scale;
+  }
+  const int64_t off = row * ep.ldy + n0;
+  if (ep.y_vec_ok && n0 + 32 <= N && ep.y_dtype != MTP_DTYPE_F32) {
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (ep.y_dtype == MTP_DTYPE_BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        packed[j] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        packed[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.y) + off);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  } else {
+    for (int j = 0; j < 32 && n0 + j < N; ++j) store_f32(ep.y, ep.y_dtype, off + j, v[j]);
+  }
+}
+
+// Argmax epilogue over 32 accumulator values, columns n0..n0+31: logit =
+// acc + bias[n]; only a strictly greater logit replaces (best, best_n), so
+// the first (lowest) index wins a tie.
+__device__ __forceinline__ void epi_argmax32(const GemmEpilogue& ep, const float (&acc)[32], int n0, int N,
+                                             int32_t& best, int& best_n) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int n = n0 + j;
+    if (n < N) {
+      float x = acc[j];
+      if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
+      const int32_t o = ordered_i32(x);
+      if (o > best) {
+        best = o;
+        best_n = n;
+      }
+    }
+  }
+}
+
+// 32 fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32_f(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
 // ab_fmt: 0 = f16, 1 = bf16 (kind::f16); FP8: E4M3 x E4M3 (kind::f8f6f4)
 template <int BN, bool FP8, int AB_FMT, int MH = 1>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -237,67 +304,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_base + (uint32_t)(acc * C::ACC_COLS + h * BN) + ((uint32_t)(q * 32) << 16);
         if (ep.mode == EPI_STORE) {
           const float rs = (ep.row_scale && row_ok) ? ep.row_scale[row] : 1.0f;
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tbase + c * 32, r);
-            tmem_wait_ld();
-            const int n0 = nb * BN + c * 32;
-            if (!row_ok || n0 >= N) continue;
             float v[32];
-  #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = n0 + j;
-              float x = __uint_as_float(r[j]) * rs;
-              if (n < N) {
-                if (ep.col_scale) x *= ep.col_scale[n];
-                if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
-              }
-              v[j] = x * ep.scale;
-            }
-            const int64_t off = (int64_t)row * ep.ldy + n0;
-            if (ep.y_vec_ok && n0 + 32 <= N && ep.y_dtype != MTP_DTYPE_F32) {
-              uint32_t packed[16];
-  #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                if (ep.y_dtype == MTP_DTYPE_BF16) {
-                  __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-                  packed[j] = *reinterpret_cast<uint32_t*>(&h);
-                } else {
-                  __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-                  packed[j] = *reinterpret_cast<uint32_t*>(&h);
-                }
-              }
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.y) + off);
-  #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-            } else {
-              for (int j = 0; j < 32 && n0 + j < N; ++j) store_f32(ep.y, ep.y_dtype, off + j, v[j]);
-            }
+            tmem_ld32_f(tbase + c * 32, v);  // every warp loads: tcgen05.ld is warp-wide
+            const int n0 = nb * BN + c * 32;
+            if (row_ok && n0 < N) epi_store32(ep, v, row, n0, N, rs);
           }
         } else {
           int32_t best = INT32_MIN;
           int best_n = nb * BN;
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tbase + c * 32, r);
-            tmem_wait_ld();
-            const int n0 = nb * BN + c * 32;
-  #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = n0 + j;
-              if (n < N) {
-                float x = __uint_as_float(r[j]);
-                if (ep.bias) x += load_f32(ep.bias, ep.bias_dtype, n);
-                const int32_t o = ordered_i32(x);
-                if (o > best) {  // strict: the first (lowest) index wins a tie
-                  best = o;
-                  best_n = n;
-                }
-              }
-            }
+            float v[32];
+            tmem_ld32_f(tbase + c * 32, v);
+            epi_argmax32(ep, v, nb * BN + c * 32, N, best, best_n);
           }
           if (row_ok) atomicMax(&ep.keys[row], make_key(best, (uint32_t)(ep.col_offset + best_n)));
         }
