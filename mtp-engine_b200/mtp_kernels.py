@@ -52,6 +52,13 @@ _HAS_TRITON = False
 
 MAX_FP8 = 448.0  # largest finite float8_e4m3fn value
 
+# Importing the reference module turns TF32 off for torch's own fp32 matmuls
+# (mtp_kernels.py:14-16), so a caller's F.linear comparisons run in full
+# fp32; the drop-in keeps that side effect.  It does not touch these kernels.
+if torch.cuda.is_available():
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+
 
 @dataclass(frozen=True)
 class KernelTuningConfig:
