@@ -93,6 +93,13 @@ int mtp_gemm_tile_rows(void);
  * tile-rows mode. */
 int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* rows, int* bn);
 
+/* Test support, host only: walks the data-parallel kernel's tile order
+ * (rows = 128 or 256, 256 columns) for every CTA of a `grid`-CTA launch and
+ * checks that each tile is taken exactly once.  *max_units (may be NULL)
+ * receives the most 128-row halves any one CTA multiplies (its load; a half
+ * tile counts 1).  MTP_OK or MTP_ERR_SHAPE (message in mtp_last_error). */
+int mtp_gemm_tile_check(int64_t M, int64_t N, int rows, int grid, int64_t* max_units);
+
 /* Process-wide choice of the paged tree-attention kernel behind
  * mtp_tree_attention_paged: 1 (default) = 128-key chunks; 2 = 64-key chunks
  * with double-buffered scores in tensor memory (shapes it cannot take run

@@ -65,6 +65,7 @@ SIGNATURES = {
     "mtp_set_gemm_tile_rows": (_i, [_i]),
     "mtp_gemm_tile_rows": (_i, []),
     "mtp_gemm_tile_plan": (_i, [_i64, _i64, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "mtp_gemm_tile_check": (_i, [_i64, _i64, _i, _i, ctypes.POINTER(_i64)]),
     "mtp_nccl_version": (_i, [ctypes.POINTER(_i)]),
     "mtp_nccl_unique_id": (_i, [_vp]),
     "mtp_nccl_comm_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i]),

@@ -598,6 +598,37 @@ int mtp_set_gemm_tile_rows(int mode) {
 
 int mtp_gemm_tile_rows(void) { return g_gemm_rows.load(std::memory_order_relaxed); }
 
+int mtp_gemm_tile_check(int64_t M, int64_t N, int rows, int grid, int64_t* max_units) {
+  if (M <= 0 || N <= 0 || grid <= 0 || (rows != 128 && rows != 256) || M > INT32_MAX / 2 || N > INT32_MAX / 2)
+    return fail(MTP_ERR_ARG, "bad tile-check arguments");
+  const int bn = 256;
+  const int num_m = (int)((M + rows - 1) / rows), num_n = (int)((N + bn - 1) / bn);
+  const int64_t num_tiles = (int64_t)num_m * num_n;
+  if (num_tiles > (1 << 26)) return fail(MTP_ERR_ARG, "too many tiles to check");
+  std::vector<uint8_t> seen((size_t)num_tiles, 0);
+  int64_t worst = 0;
+  for (int c = 0; c < grid; ++c) {
+    int64_t units = 0;  // 128-row halves this CTA multiplies
+    for (int64_t t = c, j = 0; t < num_tiles; t += grid, ++j) {
+      int mb, nb;
+      if (rows == 256) tc::tile_coords<2>((int)t, (int)j, num_m, grid, mb, nb);
+      else tc::tile_coords<1>((int)t, (int)j, num_m, grid, mb, nb);
+      if (mb < 0 || mb >= num_m || nb < 0 || nb >= num_n)
+        return fail(MTP_ERR_SHAPE, "CTA %d round %lld: tile (%d, %d) outside %d x %d", c, (long long)j, mb, nb,
+                    num_m, num_n);
+      uint8_t& s = seen[(size_t)nb * num_m + mb];
+      if (s) return fail(MTP_ERR_SHAPE, "tile (%d, %d) taken twice", mb, nb);
+      s = 1;
+      units += (rows == 256 && (int64_t)mb * 256 + 128 >= M) ? 1 : rows / 128;
+    }
+    worst = units > worst ? units : worst;
+  }
+  for (int64_t i = 0; i < num_tiles; ++i)
+    if (!seen[(size_t)i]) return fail(MTP_ERR_SHAPE, "tile %lld never taken", (long long)i);
+  if (max_units) *max_units = worst;
+  return MTP_OK;
+}
+
 int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* rows, int* bn) {
   if (M <= 0 || N <= 0 || sms <= 0 || !rows || !bn) return fail(MTP_ERR_ARG, "bad tile-plan arguments");
   const bool tall = use_tall_tiles(M, N, sms);

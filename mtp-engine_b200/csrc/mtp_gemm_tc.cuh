@@ -67,10 +67,11 @@ struct Cfg {
 // the plain order would give each CTA the same row tile in every round, so
 // the row tile is rotated by the round instead -- still a permutation of the
 // tiles of each round, and every CTA sees every row tile in turn.
+// Host and device run the same code (the host to check the order).
 template <int MH>
-__device__ __forceinline__ void tile_coords(int t, int j, int num_m, int& mb, int& nb) {
+__host__ __device__ __forceinline__ void tile_coords(int t, int j, int num_m, int grid, int& mb, int& nb) {
   nb = t / num_m;
-  if (MH == 2 && gridDim.x % num_m == 0) mb = (t + j) % num_m;
+  if (MH == 2 && grid % num_m == 0) mb = (t + j) % num_m;
   else mb = t % num_m;
 }
 
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x, j = 0; t < num_tiles && ok; t += gridDim.x, ++j) {
         int mb, nb;
-        tile_coords<MH>(t, j, num_m, mb, nb);
+        tile_coords<MH>(t, j, num_m, (int)gridDim.x, mb, nb);
         // a row half that lies wholly past M is neither loaded nor multiplied
         const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int local = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
         int mb, nb;
-        tile_coords<MH>(t, local, num_m, mb, nb);
+        tile_coords<MH>(t, local, num_m, (int)gridDim.x, mb, nb);
         const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
         const int acc = C::ACC_BUFS == 2 ? (local & 1) : 0;
         const uint32_t acc_phase = C::ACC_BUFS == 2 ? ((local >> 1) & 1) : (local & 1);
@@ -289,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int mb, nb;
-      tile_coords<MH>(t, local, num_m, mb, nb);
+      tile_coords<MH>(t, local, num_m, (int)gridDim.x, mb, nb);
       const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
       const int acc = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_phase = C::ACC_BUFS == 2 ? ((local >> 1) & 1) : (local & 1);

@@ -150,3 +150,30 @@ def test_tile_plan_choices():
         assert tile_plan(129, 64) == (256, 256) and tile_plan(128, 64)[0] == 128
     finally:
         N.set_gemm_tile_rows(before)
+
+
+def tile_check(M, Nn, rows, grid):
+    units = ctypes.c_int64(0)
+    st = N.lib().mtp_gemm_tile_check(M, Nn, rows, grid, ctypes.byref(units))
+    assert st == 0, N.lib().mtp_last_error().decode()
+    return units.value
+
+
+@pytest.mark.parametrize("M,Nn", [(384, 128256), (384, 16032), (512, 14336), (300, 1000), (129, 64),
+                                  (1000, 70000), (256, 256), (640, 9000)])
+@pytest.mark.parametrize("grid", [1, 2, 3, 7, 74, 148, 149])
+def test_tile_order_covers_every_tile_once(M, Nn, grid):
+    for rows in (128, 256):
+        tile_check(M, Nn, rows, grid)
+
+
+def test_tall_tile_rotation_balances_half_tiles():
+    """384 rows = one full and one half row tile per weight tile: on 148
+    CTAs the rotated order gives every CTA both in turn, so no CTA carries
+    more than its share (the plain order would give the even CTAs every full
+    tile: 2 units per round instead of 1.5)."""
+    tiles = 2 * -(-128256 // 256)          # 1002 tiles of 256 x 256
+    rounds = -(-tiles // SMS)              # 7
+    worst = tile_check(384, 128256, 256, SMS)
+    assert worst <= (rounds // 2 + 1) * 2 + (rounds // 2)  # 4 full + 3 half = 11 units
+    assert worst < 2 * rounds                               # below the unrotated 14
