@@ -41,6 +41,20 @@ def _worker(rank, world, port, case, q):
         if case == "tie_across_shards":
             lo1, _ = O.vocab_shard_bounds(w.shape[0], world)[1]
             w[lo1 + 3] = w[2]  # equal logits in rank 0 and rank 1 blocks: index 2 must win
+        if case == "weak":
+            # each rank holds only its own sequences; the candidates of every
+            # rank are all-gathered (asynchronously, as the weak-scaling bench
+            # does) before the vocabulary-sharded argmax
+            bs = h.shape[0] // world
+            h_loc = torch.from_numpy(np.ascontiguousarray(h[rank * bs:(rank + 1) * bs]))
+            d_loc = torch.from_numpy(np.ascontiguousarray(d[rank * bs:(rank + 1) * bs]).astype(np.int32))
+            h_all = torch.empty((bs * world,) + h_loc.shape[1:], dtype=h_loc.dtype)
+            d_all = torch.empty((bs * world,) + d_loc.shape[1:], dtype=d_loc.dtype)
+            works = [dist.all_gather_into_tensor(h_all, h_loc, async_op=True),
+                     dist.all_gather_into_tensor(d_all, d_loc, async_op=True)]
+            for wk in works:
+                wk.wait()
+            h, d = h_all.numpy(), d_all.numpy()
         B, S, K = h.shape
         lo, hi = O.vocab_shard_bounds(w.shape[0], world)[rank]
         keys = O.shard_argmax_keys(h.reshape(B * S, K), w[lo:hi], None, lo)
@@ -102,3 +116,19 @@ def test_dead_rank_surfaces_as_error():
     out = _run(2, "dead_rank", 1)
     status, payload, _ = out[0]
     assert status == "error", "the surviving rank should see the collective fail"
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_weak_scaling_exchange(world):
+    """The weak-scaling bench's data flow: every rank owns 6 / world of the
+    sequences, all-gathers the candidates, folds its vocabulary block into
+    keys and all-reduces them; every rank must then hold single-device
+    verification of all sequences."""
+    g = np.load(GOLDEN)
+    full = O.fused_multi_verify(g["h3"], g["w3"], None, g["d3"])
+    out = _run(world, "weak", world)
+    for r in range(world):
+        status, payload, _ = out[r]
+        assert status == "ok", payload
+        for a, b in zip(payload, full):
+            np.testing.assert_array_equal(np.asarray(a), b)
