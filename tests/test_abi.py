@@ -177,3 +177,26 @@ def test_decode_kernel_switch_roundtrip():
         assert N.lib().mtp_set_decode_kernel(0) == 8  # MTP_ERR_ARG
     finally:
         N.set_decode_kernel(before)
+
+
+def test_c_host_program(tmp_path):
+    """A plain C99 program compiled against include/mtp_b200.h alone links
+    libmtp_b200.so and drives the entry points that need no GPU
+    (tests/c_host/abi_host.c): the header is valid C and the boundary is
+    usable without Python."""
+    import shutil
+    import subprocess
+    import _mtp_native as N
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    repo = REPO
+    N.lib()  # builds the library when it is missing
+    libdir = os.path.join(repo, "mtp-engine_b200")
+    exe = str(tmp_path / "abi_host")
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(repo, "include"),
+                        os.path.join(repo, "tests", "c_host", "abi_host.c"), "-L", libdir, "-lmtp_b200",
+                        f"-Wl,-rpath,{libdir}", "-o", exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
