@@ -1,11 +1,13 @@
-"""The synchronisation protocols of two kernels that have not yet run on a
+"""The synchronisation protocols of kernels that have not yet run on a
 GPU, checked on the CPU with randomised interleaving models
-(tests/protocol_models.py): the 64-key tree attention's mbarrier protocol
-the vocab-parallel peer-memory key exchange, and the exchange fused into
-the shard GEMM.  Each model must be clean
+(tests/protocol_models.py): the 64-key tree attention's mbarrier protocol,
+the vocab-parallel peer-memory key exchange, the exchange fused into the
+shard GEMM, and the GEMM's accumulator handshake with one or two buffers.  Each model must be clean
 for the protocol the kernel uses and must catch a known-bad variant (the
 previous final wait of the attention kernel; one parity for the exchange),
 which shows the model can see the bug it guards against."""
+
+import pytest
 
 import protocol_models as PM
 
@@ -40,3 +42,25 @@ def test_fused_exchange_protocol():
     run = lambda par: (lambda seed: PM.run_fused_exchange(seed, 2 + seed % 7, 6, parities=par))
     assert _count(run(2), range(300)) == 0
     assert _count(run(1), range(300)) > 0
+
+
+@pytest.mark.parametrize("acc_bufs", [1, 2])
+def test_gemm_accumulator_handshake(acc_bufs):
+    """gemm_tc_kernel: double-buffered accumulators (128-row tiles) and the
+    single accumulator of the 256-row tiles -- every MMA reads the stage it
+    expects and the epilogue reads each tile's complete accumulator."""
+    for seed in range(150):
+        PM.run_gemm(seed, n_tiles=7, num_kb=5, stages=3, acc_bufs=acc_bufs)
+        PM.run_gemm(seed + 1000, n_tiles=4, num_kb=1, stages=2, acc_bufs=acc_bufs)
+
+
+def test_gemm_model_flags_wrong_single_buffer_phases():
+    """Control: the double-buffer phase formula on a single accumulator must
+    be caught (a wait passing early, a stale read, or a deadlock)."""
+    flagged = 0
+    for seed in range(50):
+        try:
+            PM.run_gemm(seed, n_tiles=7, num_kb=5, stages=3, acc_bufs=1, phase_rule="double")
+        except PM.Violation:
+            flagged += 1
+    assert flagged == 50
