@@ -652,6 +652,33 @@ def run_sweep(args):
         N.set_gemm_tile_rows(base_rows)
         return out
 
+    # ---- config 1: the CPU-runnable chain (fp32, seed 0): RMSNorm-linear of the
+    # 5 candidate positions, then fused_multi_verify with the first two drafts
+    # set to the target's own argmax -> accepted_n = 2 (launch-bound; bytes =
+    # both weights once)
+    g1 = torch.Generator(device=dev).manual_seed(0)
+    x1 = torch.randn(1, 5, 256, generator=g1, device=dev)
+    gam1 = 1.0 + 0.1 * torch.randn(256, generator=g1, device=dev)
+    W1 = 0.02 * torch.randn(256, 256, generator=g1, device=dev)
+    LM1 = 0.02 * torch.randn(4096, 256, generator=g1, device=dev)
+    y1 = mk.fused_rmsnorm_linear(x1[0], W1, None, 1e-6, norm_weight=gam1)
+    top1 = (y1 @ LM1.T).argmax(-1)
+    d1 = torch.randint(0, 4096, (1, 4), generator=g1, device=dev, dtype=torch.int32)
+    d1[0, :2] = top1[1:3].to(torch.int32)
+    if int(top1[3]) == int(d1[0, 2]):
+        d1[0, 2] = (d1[0, 2] + 1) % 4096
+    chain1 = lambda: mv.fused_multi_verify(mk.fused_rmsnorm_linear(x1[0], W1, None, 1e-6, norm_weight=gam1)[None],
+                                           LM1, d1)
+    n1 = int(chain1()[1][0])
+    t1 = time_call(chain1, iters)
+    xs1, ws1, gs1, lms1, ds1 = f32(x1[0]), f32(W1), f32(gam1), f32(LM1), d1.cpu().numpy()
+    ct = cpu_time(lambda: O.fused_multi_verify(O.rmsnorm_linear(xs1, ws1 * gs1[None, :], None, 1e-6, 1.0)[None],
+                                               lms1, None, ds1))
+    emit("config1_chain", 5, "verified candidates/s", t1, "hbm", 4.0 * (256 * 256 + 4096 * 256) / t1 / 1e9,
+         peaks["hbm"], "measured hbm_gbs", 5, ct, {"dtype": "f32", "accepted_n": n1,
+                                                   "note": "launch-bound: two launches for 4.5 MB"})
+    del x1, W1, LM1
+
     # ---- config 2 sweep: RMSNorm-linear bf16, gamma on
     for M in (64, 512, 2048, 8192):
         K, Nn = C2["K"], C2["N"]
