@@ -51,7 +51,9 @@ extern "C" {
 /* ABI version of this header (bumped on any signature change). */
 int mtp_abi_version(void);
 
-/* Thread-local description of the last failing call on this thread. */
+/* Thread-local description of the last failing call on this thread (the
+ * reference raises AssertionError from its wrappers instead, e.g.
+ * mtp_kernels.py:949; the Python layer here raises from this text). */
 const char* mtp_last_error(void);
 
 /* Synchronises `stream`, then reports the current device's error word
@@ -171,7 +173,8 @@ int mtp_rmsnorm_linear(const void* x, int x_dtype, const void* weight, int w_dty
                        void* y, int y_dtype, int64_t M, int64_t N, int64_t K, float eps,
                        float scale, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Bytes of workspace mtp_rmsnorm_linear_fp8 needs for these sizes. */
+/* Bytes of workspace mtp_rmsnorm_linear_fp8 needs for these sizes
+ * (caller-provided scratch; the reference allocates inside the call). */
 size_t mtp_rmsnorm_linear_fp8_workspace(int64_t M, int64_t K);
 
 /* y[M,N] = rmsnorm(x) @ (W * wscale[:,None])^T + bias.
@@ -235,7 +238,8 @@ int mtp_paged_attention(const void* q, const void* k_pages, const void* v_pages,
                         int64_t L, int64_t D, int64_t num_pages, int64_t page_size, float scale,
                         void* stream);
 
-/* Bytes of workspace mtp_tree_attention_paged needs. */
+/* Bytes of workspace mtp_tree_attention_paged needs (caller-provided
+ * scratch for split keys; no counterpart in the reference). */
 size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv,
                                           int64_t D, int64_t ctx_len);
 
@@ -445,6 +449,9 @@ int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* 
  * to INT64_MIN.  epoch is a device uint64 that starts at 0 on every rank;
  * all ranks must make the same sequence of calls. */
 size_t mtp_verify_exchange_bytes(int64_t rows, int world);
+int mtp_verify_exchange_chain(int64_t* keys, const void* peer_bufs, int rank, int world, uint64_t* epoch,
+                              const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected,
+                              int64_t B, int64_t S, void* stream);
 
 /* Vocab-parallel verify as ONE kernel per rank, the all-reduce fused into the
  * shard GEMM (replaces mtp_verify_shard_keys + the all-reduce + the scan,
@@ -482,11 +489,9 @@ int mtp_verify_shard_fused(const void* hidden, int h_dtype, const void* weight_s
  * recommended (ld >= D accepted), info [2] int32.  One small launch. */
 int mtp_verify_step(const int32_t* draft, const int32_t* accepted_n, const int32_t* corrected, int64_t B, int64_t D,
                     int32_t* step_tokens, int64_t ld, int32_t* info, void* stream);
-int mtp_verify_exchange_chain(int64_t* keys, const void* peer_bufs, int rank, int world, uint64_t* epoch,
-                              const int32_t* draft, int8_t* accept, int32_t* accepted_n, int32_t* corrected,
-                              int64_t B, int64_t S, void* stream);
 
-/* Fills keys[n] with INT64_MIN. */
+/* Fills keys[n] with INT64_MIN (workspace plumbing; no counterpart in the
+ * reference, whose temporaries are allocated inside each call). */
 int mtp_keys_fill(int64_t* keys, int64_t n, void* stream);
 
 /* Number of kernels this library has launched in this process (all
