@@ -400,8 +400,9 @@ size_t mtp_vocab_parallel_workspace(int64_t B, int64_t S, int64_t V_shard, int64
 /* One rank's vocab-parallel fused_multi_verify in one call: this rank's
  * block [vocab_offset, vocab_offset + V_shard) of the lm_head folded into
  * argmax keys (mtp_verify_shard_keys_ws), the keys all-reduced with MAX
- * over `comm` (ncclInt64, in place; no collective when comm is NULL, a
- * single-rank run), then decoded into accept [B, S-1] int8, accepted_n [B]
+ * over `comm` (ncclInt64, in place; every call with a communicator runs it,
+ * a one-rank communicator included; comm NULL = a single-rank run with no
+ * collective), then decoded into accept [B, S-1] int8, accepted_n [B]
  * and corrected [B] int32 -- identical on every rank and equal to
  * mtp_fused_multi_verify over the whole lm_head (mtp_fused_verify.py:
  * 237-290 with the weight split as torch.chunk splits it,

@@ -1824,8 +1824,8 @@ int mtp_vocab_parallel_multi_verify(const void* hidden, int h_dtype, const void*
                                           workspace_bytes - keys_bytes, stream))
       return st;
   }
-  if (c && c->world > 1)
-    MTP_NCCL_TRY(nccl::api().AllReduce(keys, keys, (size_t)rows, ncclInt64, ncclMax, c->comm, s));
+  // with a communicator the collective always runs (a one-rank communicator reduces locally)
+  if (c) MTP_NCCL_TRY(nccl::api().AllReduce(keys, keys, (size_t)rows, ncclInt64, ncclMax, c->comm, s));
   return mtp_verify_chain_from_keys(keys, draft, accept, accepted_n, corrected, B, S, stream);
 }
 
