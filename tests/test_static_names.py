@@ -14,7 +14,10 @@ from conftest import REPO
 
 FILES = ["bench.py", "__graft_entry__.py", "mtp-engine_b200/_mtp_native.py", "mtp-engine_b200/mtp_kernels.py",
          "mtp-engine_b200/mtp_fused_verify.py", "mtp-engine_b200/mtp_parallel.py",
-         "mtp-engine_b200/mtp_draft_tree.py", "mtp-engine_b200/_build.py"]
+         "mtp-engine_b200/mtp_draft_tree.py", "mtp-engine_b200/_build.py", "oracle/mtp_oracle.py"]
+# the GPU tests too: on a CPU they are collected but never run
+FILES += sorted(os.path.join("tests", f) for f in os.listdir(os.path.join(REPO, "tests"))
+                if f.startswith("test_") and f.endswith(".py"))
 MODULE_DUNDERS = {"__file__", "__name__", "__doc__", "__spec__", "__loader__", "__package__", "__path__"}
 
 
