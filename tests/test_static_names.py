@@ -42,3 +42,58 @@ def unresolved(path):
 @pytest.mark.parametrize("path", FILES)
 def test_every_name_resolves(path):
     assert unresolved(path) == []
+
+
+PROJECT_MODULES = {"_mtp_native", "mtp_kernels", "mtp_fused_verify", "mtp_parallel", "mtp_draft_tree",
+                   "oracle.mtp_oracle", "protocol_models"}
+
+
+def bad_attributes(path):
+    """`alias.name` uses, where alias is an imported project module (at any
+    scope), naming something the module does not define."""
+    import ast
+    import importlib
+    tree = ast.parse(open(os.path.join(REPO, path)).read())
+    aliases = {}
+    for node in ast.walk(tree):
+        if isinstance(node, ast.Import):
+            for a in node.names:
+                if a.name in PROJECT_MODULES:
+                    aliases[a.asname or a.name] = a.name
+        elif isinstance(node, ast.ImportFrom) and node.module == "oracle":
+            for a in node.names:
+                if a.name == "mtp_oracle":
+                    aliases[a.asname or a.name] = "oracle.mtp_oracle"
+    # uses inside `with pytest.raises(...)` are meant to fail (out-of-scope names)
+    expected = set()
+    for node in ast.walk(tree):
+        if isinstance(node, ast.With) and any(
+                isinstance(i.context_expr, ast.Call) and isinstance(i.context_expr.func, ast.Attribute)
+                and i.context_expr.func.attr == "raises" for i in node.items):
+            expected.update(id(n) for stmt in node.body for n in ast.walk(stmt))
+    out = []
+    for node in ast.walk(tree):
+        if id(node) in expected:
+            continue
+        if isinstance(node, ast.Attribute) and isinstance(node.value, ast.Name) and node.value.id in aliases:
+            mod = importlib.import_module(aliases[node.value.id])
+            if not hasattr(mod, node.attr):
+                out.append(f"{path}:{node.lineno}: {node.value.id}.{node.attr}")
+    return out
+
+
+@pytest.mark.parametrize("path", FILES)
+def test_project_attributes_exist(path):
+    assert bad_attributes(path) == []
+
+
+@pytest.mark.parametrize("path", FILES)
+def test_library_calls_have_signatures(path):
+    """Every C entry point the Python side calls (`....mtp_name`) has its
+    argument and result types in _mtp_native.SIGNATURES: without them ctypes
+    would pass 64-bit sizes and pointers as C ints."""
+    import re
+    import _mtp_native as N
+    src = open(os.path.join(REPO, path)).read()
+    used = set(re.findall(r"\.(mtp_[a-z0-9_]+)\s*\(", src))  # calls only
+    assert sorted(used - set(N.SIGNATURES)) == []
