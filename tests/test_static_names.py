@@ -97,3 +97,68 @@ def test_library_calls_have_signatures(path):
     src = open(os.path.join(REPO, path)).read()
     used = set(re.findall(r"\.(mtp_[a-z0-9_]+)\s*\(", src))  # calls only
     assert sorted(used - set(N.SIGNATURES)) == []
+
+
+@pytest.mark.parametrize("path", FILES)
+def test_library_call_arity(path):
+    """Each call of a C entry point passes as many arguments as the header
+    declares (ctypes would raise only when the call runs -- on a GPU for
+    most of them)."""
+    import ast
+    import _mtp_native as N
+    tree = ast.parse(open(os.path.join(REPO, path)).read())
+    bad = []
+    for node in ast.walk(tree):
+        if (isinstance(node, ast.Call) and isinstance(node.func, ast.Attribute)
+                and node.func.attr in N.SIGNATURES
+                and not any(isinstance(a, ast.Starred) for a in node.args) and not node.keywords):
+            want = len(N.SIGNATURES[node.func.attr][1])
+            if len(node.args) != want:
+                bad.append(f"{path}:{node.lineno}: {node.func.attr} with {len(node.args)} arguments, declared {want}")
+    assert bad == []
+
+
+def header_declarations():
+    import re
+    src = open(os.path.join(REPO, "include", "mtp_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    decls = {}
+    for ret, name, params in re.findall(r"\b(int|size_t|const char\*|uint64_t)\s+(mtp_[a-z0-9_]+)\s*\(([^)]*)\)\s*;",
+                                        src):
+        ps = [p.strip() for p in params.split(",") if p.strip() and p.strip() != "void"]
+        decls[name] = (ret, ps)
+    return decls
+
+
+def test_binding_types_match_header():
+    """_mtp_native.SIGNATURES against include/mtp_b200.h, parameter by
+    parameter: pointers as pointers, int64_t as c_int64, size_t as c_size_t,
+    int as c_int, float as c_float, and the result type."""
+    import ctypes
+    import _mtp_native as N
+
+    def kind_c(p):
+        if "*" in p:
+            return "ptr"
+        t = p.split()[0] if not p.startswith("const") else p.split()[1]
+        return {"int64_t": "i64", "size_t": "u64", "int": "int", "float": "float", "uint64_t": "u64"}[t]
+
+    def kind_py(t):
+        if t in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(t, type) and issubclass(t, ctypes._Pointer)):
+            return "ptr"
+        # c_size_t is c_uint64 on this ABI (LP64)
+        return {ctypes.c_int64: "i64", ctypes.c_size_t: "u64", ctypes.c_int: "int", ctypes.c_float: "float",
+                ctypes.c_uint64: "u64"}[t]
+
+    decls = header_declarations()
+    assert sorted(decls) == sorted(N.SIGNATURES)
+    bad = []
+    for name, (ret, params) in decls.items():
+        rt, argtypes = N.SIGNATURES[name]
+        want_ret = {"int": ctypes.c_int, "size_t": ctypes.c_size_t, "const char*": ctypes.c_char_p,
+                    "uint64_t": ctypes.c_uint64}[ret]
+        if rt is not want_ret:
+            bad.append(f"{name}: result {rt} vs {ret}")
+        if [kind_c(p) for p in params] != [kind_py(t) for t in argtypes]:
+            bad.append(f"{name}: {[kind_c(p) for p in params]} vs {[kind_py(t) for t in argtypes]}")
+    assert bad == []
