@@ -1,11 +1,13 @@
-"""The peer-memory key exchange kernel (mtp_verify_exchange_chain) on one
-GPU.  With world = 1 it must reproduce fused_multi_verify (push, flag, wait
-on its own flag, decode) call after call.  With world = 2 and a second
-buffer that no rank ever signals -- a flag that nothing sets -- the bounded
-wait must run out (2 s), the kernel must return with MTP_ERR_TIMEOUT in the
-device status and the keys back at rest, and the context must stay usable
-for the next operator.  No second kernel waits on this one.  GPU only; runs
-in a child process (tests/test_gpu_isolated.py)."""
+"""The two peer-memory exchanges on one GPU: the exchange kernel
+(mtp_verify_exchange_chain) and the shard GEMM with the exchange fused in
+(mtp_verify_shard_fused).  With world = 1 each must reproduce
+fused_multi_verify (keys to its own buffer, flag itself, decode) call after
+call.  With world = 2 and a second buffer that no rank ever signals -- a
+flag that nothing sets -- the bounded wait must run out (2 s), the kernel
+must return with MTP_ERR_TIMEOUT in the device status and its keys back at
+rest, and the context must stay usable for the next operator.  No second
+kernel waits on these.  GPU only; runs in a child process
+(tests/test_gpu_isolated.py)."""
 
 import time
 
@@ -103,3 +105,63 @@ def test_missing_peer_times_out_and_context_survives(mods):
     torch.cuda.synchronize()
     assert N.device_status(dev) == 0
     assert int(ref[1].min()) >= 0
+
+
+def fused_buffers(N, rows, world, count):
+    d = torch.device("cuda", 0)
+    nbytes = N.lib().mtp_verify_fused_bytes(rows, world)
+    bufs = [torch.empty(-(-nbytes // 8), dtype=torch.int64, device=d) for _ in range(count)]
+    for b in bufs:
+        N.check(N.lib().mtp_verify_fused_init(N.ptr(b), rows, world, N.stream_handle(d)), "fused init")
+    peers = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=d)
+    return bufs, peers
+
+
+def shard_fused(N, hid, w, draft, peers, rank, world):
+    B, S, K = hid.shape
+    d = hid.device
+    ws = N.verify_workspace(d, 0, w.shape[0], K, N.DT_BF16)
+    acc = torch.full((B, S - 1), -1, dtype=torch.int8, device=d)
+    n = torch.full((B,), -1, dtype=torch.int32, device=d)
+    c = torch.full((B,), -1, dtype=torch.int32, device=d)
+    N.check(N.lib().mtp_verify_shard_fused(N.ptr(hid), N.DT_BF16, N.ptr(w), N.DT_BF16, None, 0, N.ptr(peers), rank,
+                                           world, N.ptr(draft), N.ptr(acc), N.ptr(n), N.ptr(c), B, S, K, w.shape[0],
+                                           0, N.ptr(ws), ws.numel(), N.stream_handle(d)), "mtp_verify_shard_fused")
+    return acc, n, c
+
+
+def test_fused_exchange_single_rank_matches_verify(mods):
+    """The GEMM with the exchange fused in, world = 1: every tile's keys go
+    to this rank's own buffer, the last CTA flags itself and decodes."""
+    N, mv = mods
+    hid, w, draft = inputs(3)
+    B, S, _ = hid.shape
+    ref = mv.fused_multi_verify(hid, w, draft)
+    bufs, peers = fused_buffers(N, B * S, 1, 1)
+    for _ in range(3):  # both key parities, then the first again
+        got = shard_fused(N, hid, w, draft, peers, 0, 1)
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)
+    assert N.device_status(hid.device) == 0
+
+
+def test_fused_exchange_missing_peer_times_out(mods):
+    N, mv = mods
+    hid, w, draft = inputs(4)
+    B, S, _ = hid.shape
+    dev = hid.device
+    N.device_status(dev)
+    bufs, peers = fused_buffers(N, B * S, 2, 2)  # rank 1 never runs
+    t0 = time.perf_counter()
+    shard_fused(N, hid, w, draft, peers, 0, 2)
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert N.device_status(dev) == ERR_TIMEOUT
+    assert 1.0 < waited < 30.0
+    # this rank's keys of the failed call are back at rest, and the context works
+    rows = B * S
+    assert bool((bufs[0][:2 * rows] == INT64_MIN).all())
+    ref = mv.fused_multi_verify(hid, w, draft)
+    torch.cuda.synchronize()
+    assert N.device_status(dev) == 0 and int(ref[1].min()) >= 0
