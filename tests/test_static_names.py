@@ -162,3 +162,17 @@ def test_binding_types_match_header():
         if [kind_c(p) for p in params] != [kind_py(t) for t in argtypes]:
             bad.append(f"{name}: {[kind_c(p) for p in params]} vs {[kind_py(t) for t in argtypes]}")
     assert bad == []
+
+
+def test_product_never_uses_the_oracle():
+    """The oracle is test infrastructure: nothing in the product package
+    imports, loads or names it (the product has no CPU fallback)."""
+    pkg = os.path.join(REPO, "mtp-engine_b200")
+    hits = []
+    for root, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".h")):
+                src = open(os.path.join(root, f)).read()
+                if "oracle" in src or "mtp_oracle" in src:
+                    hits.append(os.path.relpath(os.path.join(root, f), REPO))
+    assert hits == []
