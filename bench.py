@@ -761,6 +761,25 @@ def run_sweep(args):
              "measured bf16_tflops_sustained", 2 * S, ct, {"gemm_schedule": v})
     del lm
 
+    # ---- the reference's own verify benchmark geometry (bench_optimizations.py:58-113):
+    # B=32, S=5, K=256, V=8192 with bias, fp32 (the CUDA-core exact-fp32 GEMM) and bf16
+    for dt in (torch.float32, torch.bfloat16):
+        g = torch.Generator(device=dev).manual_seed(0)
+        hr = torch.randn(32, 5, 256, generator=g, device=dev).to(dt)
+        wr = torch.randn(8192, 256, generator=g, device=dev).to(dt)
+        br = torch.randn(8192, generator=g, device=dev)
+        dr_ = torch.randint(0, 8192, (32, 4), generator=g, device=dev, dtype=torch.int32)
+        t = time_call(lambda: mv.fused_multi_verify(hr, wr, dr_, br), iters)
+        hs_, ws2, bs_, ds_ = f32(hr[:4]), f32(wr), f32(br), dr_[:4].cpu().numpy()
+        ct = cpu_time(lambda: O.fused_multi_verify(hs_, ws2, bs_, ds_))
+        flop = 2.0 * 32 * 5 * 256 * 8192
+        emit(f"ref_bench_fusion_verify_{'fp32' if dt == torch.float32 else 'bf16'}", 32 * 5,
+             "verified candidates/s", t, "tensor", flop / t / 1e12, peaks["bf16"],
+             "measured bf16_tflops (burst)", 4 * 5, ct,
+             {"dtype": "f32" if dt == torch.float32 else "bf16",
+              "note": "launch-bound size (0.34 GFLOP); the reference times it at bench_optimizations.py:58-113"})
+        del hr, wr
+
     # ---- operators around the path (not BASELINE configs): one line each
     # tree attention -> RMSNorm -> linear: the reference's own bench geometry
     # (bench_memory.py:96, fp32) and a draft-head shape (bf16, D = hidden)
