@@ -652,224 +652,242 @@ def run_sweep(args):
         N.set_gemm_tile_rows(base_rows)
         return out
 
-    # ---- config 1: the CPU-runnable chain (fp32, seed 0): RMSNorm-linear of the
-    # 5 candidate positions, then fused_multi_verify with the first two drafts
-    # set to the target's own argmax -> accepted_n = 2 (launch-bound; bytes =
-    # both weights once)
-    g1 = torch.Generator(device=dev).manual_seed(0)
-    x1 = torch.randn(1, 5, 256, generator=g1, device=dev)
-    gam1 = 1.0 + 0.1 * torch.randn(256, generator=g1, device=dev)
-    W1 = 0.02 * torch.randn(256, 256, generator=g1, device=dev)
-    LM1 = 0.02 * torch.randn(4096, 256, generator=g1, device=dev)
-    y1 = mk.fused_rmsnorm_linear(x1[0], W1, None, 1e-6, norm_weight=gam1)
-    top1 = (y1 @ LM1.T).argmax(-1)
-    d1 = torch.randint(0, 4096, (1, 4), generator=g1, device=dev, dtype=torch.int32)
-    d1[0, :2] = top1[1:3].to(torch.int32)
-    if int(top1[3]) == int(d1[0, 2]):
-        d1[0, 2] = (d1[0, 2] + 1) % 4096
-    chain1 = lambda: mv.fused_multi_verify(mk.fused_rmsnorm_linear(x1[0], W1, None, 1e-6, norm_weight=gam1)[None],
-                                           LM1, d1)
-    n1 = int(chain1()[1][0])
-    t1 = time_call(chain1, iters)
-    xs1, ws1, gs1, lms1, ds1 = f32(x1[0]), f32(W1), f32(gam1), f32(LM1), d1.cpu().numpy()
-    ct = cpu_time(lambda: O.fused_multi_verify(O.rmsnorm_linear(xs1, ws1 * gs1[None, :], None, 1e-6, 1.0)[None],
-                                               lms1, None, ds1))
-    emit("config1_chain", 5, "verified candidates/s", t1, "hbm", 4.0 * (256 * 256 + 4096 * 256) / t1 / 1e9,
-         peaks["hbm"], "measured hbm_gbs", 5, ct, {"dtype": "f32", "accepted_n": n1,
-                                                   "note": "launch-bound: two launches for 4.5 MB"})
-    del x1, W1, LM1
+    def sec_config1():
+        # ---- config 1: the CPU-runnable chain (fp32, seed 0): RMSNorm-linear of the
+        # 5 candidate positions, then fused_multi_verify with the first two drafts
+        # set to the target's own argmax -> accepted_n = 2 (launch-bound; bytes =
+        # both weights once)
+        g1 = torch.Generator(device=dev).manual_seed(0)
+        x1 = torch.randn(1, 5, 256, generator=g1, device=dev)
+        gam1 = 1.0 + 0.1 * torch.randn(256, generator=g1, device=dev)
+        W1 = 0.02 * torch.randn(256, 256, generator=g1, device=dev)
+        LM1 = 0.02 * torch.randn(4096, 256, generator=g1, device=dev)
+        y1 = mk.fused_rmsnorm_linear(x1[0], W1, None, 1e-6, norm_weight=gam1)
+        top1 = (y1 @ LM1.T).argmax(-1)
+        d1 = torch.randint(0, 4096, (1, 4), generator=g1, device=dev, dtype=torch.int32)
+        d1[0, :2] = top1[1:3].to(torch.int32)
+        if int(top1[3]) == int(d1[0, 2]):
+            d1[0, 2] = (d1[0, 2] + 1) % 4096
+        chain1 = lambda: mv.fused_multi_verify(mk.fused_rmsnorm_linear(x1[0], W1, None, 1e-6, norm_weight=gam1)[None],
+                                               LM1, d1)
+        n1 = int(chain1()[1][0])
+        t1 = time_call(chain1, iters)
+        xs1, ws1, gs1, lms1, ds1 = f32(x1[0]), f32(W1), f32(gam1), f32(LM1), d1.cpu().numpy()
+        ct = cpu_time(lambda: O.fused_multi_verify(O.rmsnorm_linear(xs1, ws1 * gs1[None, :], None, 1e-6, 1.0)[None],
+                                                   lms1, None, ds1))
+        emit("config1_chain", 5, "verified candidates/s", t1, "hbm", 4.0 * (256 * 256 + 4096 * 256) / t1 / 1e9,
+             peaks["hbm"], "measured hbm_gbs", 5, ct, {"dtype": "f32", "accepted_n": n1,
+                                                       "note": "launch-bound: two launches for 4.5 MB"})
+        del x1, W1, LM1
 
-    # ---- config 2 sweep: RMSNorm-linear bf16, gamma on
-    for M in (64, 512, 2048, 8192):
-        K, Nn = C2["K"], C2["N"]
-        g = torch.Generator(device=dev).manual_seed(1)
-        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
-        gam = 1.0 + 0.1 * torch.randn(K, generator=g, device=dev)
-        W = (0.02 * torch.randn(Nn, K, generator=g, device=dev)).to(torch.bfloat16)
-        times = timed_gemm(lambda: mk.fused_rmsnorm_linear(x, W, None, C2["eps"], norm_weight=gam))
-        flop, byts = 2.0 * M * Nn * K, 2.0 * (M * K + Nn * K + M * Nn)
-        tensor = flop / byts > 281  # ridge of the measured peaks
-        rows = min(M, 16)
-        xs, ws, gs = f32(x[:rows]), f32(W), f32(gam)
-        ct = cpu_time(lambda: O.rmsnorm_linear(xs, ws * gs[None, :], None, C2["eps"], 1.0))
+    def sec_config2():
+        # ---- config 2 sweep: RMSNorm-linear bf16, gamma on
+        for M in (64, 512, 2048, 8192):
+            K, Nn = C2["K"], C2["N"]
+            g = torch.Generator(device=dev).manual_seed(1)
+            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            gam = 1.0 + 0.1 * torch.randn(K, generator=g, device=dev)
+            W = (0.02 * torch.randn(Nn, K, generator=g, device=dev)).to(torch.bfloat16)
+            times = timed_gemm(lambda: mk.fused_rmsnorm_linear(x, W, None, C2["eps"], norm_weight=gam))
+            flop, byts = 2.0 * M * Nn * K, 2.0 * (M * K + Nn * K + M * Nn)
+            tensor = flop / byts > 281  # ridge of the measured peaks
+            rows = min(M, 16)
+            xs, ws, gs = f32(x[:rows]), f32(W), f32(gam)
+            ct = cpu_time(lambda: O.rmsnorm_linear(xs, ws * gs[None, :], None, C2["eps"], 1.0))
+            for v, t in times:
+                emit(f"config2_M{M}", M, "rows/s", t, "tensor" if tensor else "hbm",
+                     flop / t / 1e12 if tensor else byts / t / 1e9, peaks["bf16_sus"] if tensor else peaks["hbm"],
+                     "measured bf16_tflops_sustained" if tensor else "measured hbm_gbs", rows, ct,
+                     {"gemm_schedule": v})
+            del x, W
+
+    def sec_config3():
+        # ---- config 3: FP8 E4M3, per-token activations, packed per-channel weight scales
+        M, K, Nn = 1024, 8192, 28672
+        g = torch.Generator(device=dev).manual_seed(2)
+        x = torch.randn(M, K, generator=g, device=dev)
+        x = x * (448.0 / x.abs().amax(dim=1, keepdim=True))
+        xq, sx = mk.quantize_fp8_rows(x)
+        wq, sw = mk.quantize_fp8_rows(0.02 * torch.randn(Nn, K, generator=g, device=dev))
+        flat, offs = mk.pack_scales([sw])
+        swv = mk.unpack_scale_tensor(flat, offs, 0, (Nn,))
+        times = timed_gemm(lambda: mk.fused_rmsnorm_linear_fp8(xq, wq, swv, x_scale=sx, out_dtype=torch.bfloat16))
+        flop = 2.0 * M * Nn * K
+        rows = 4
+        xd = O.e4m3_bits_to_f32(xq[:rows].view(torch.uint8).cpu().numpy()) * f32(sx)[:rows, None]
+        wd = O.e4m3_bits_to_f32(wq.view(torch.uint8).cpu().numpy())
+        sws = f32(sw)
+        ct = cpu_time(lambda: O.rmsnorm_linear_fp8(xd, wd, sws, None, 1e-6))
         for v, t in times:
-            emit(f"config2_M{M}", M, "rows/s", t, "tensor" if tensor else "hbm",
-                 flop / t / 1e12 if tensor else byts / t / 1e9, peaks["bf16_sus"] if tensor else peaks["hbm"],
-                 "measured bf16_tflops_sustained" if tensor else "measured hbm_gbs", rows, ct,
-                 {"gemm_schedule": v})
-        del x, W
-    # ---- config 3: FP8 E4M3, per-token activations, packed per-channel weight scales
-    M, K, Nn = 1024, 8192, 28672
-    g = torch.Generator(device=dev).manual_seed(2)
-    x = torch.randn(M, K, generator=g, device=dev)
-    x = x * (448.0 / x.abs().amax(dim=1, keepdim=True))
-    xq, sx = mk.quantize_fp8_rows(x)
-    wq, sw = mk.quantize_fp8_rows(0.02 * torch.randn(Nn, K, generator=g, device=dev))
-    flat, offs = mk.pack_scales([sw])
-    swv = mk.unpack_scale_tensor(flat, offs, 0, (Nn,))
-    times = timed_gemm(lambda: mk.fused_rmsnorm_linear_fp8(xq, wq, swv, x_scale=sx, out_dtype=torch.bfloat16))
-    flop = 2.0 * M * Nn * K
-    rows = 4
-    xd = O.e4m3_bits_to_f32(xq[:rows].view(torch.uint8).cpu().numpy()) * f32(sx)[:rows, None]
-    wd = O.e4m3_bits_to_f32(wq.view(torch.uint8).cpu().numpy())
-    sws = f32(sw)
-    ct = cpu_time(lambda: O.rmsnorm_linear_fp8(xd, wd, sws, None, 1e-6))
-    for v, t in times:
-        emit("config3_fp8", M, "rows/s", t, "tensor", flop / t / 1e12, 2 * peaks["bf16_sus"],
-             "2 x measured bf16_tflops_sustained (nominal fp8:bf16 ratio; fp8 not measured)", rows, ct,
-             {"dtype": "e4m3", "gemm_schedule": v})
-    del x, xq, wq
-    # ---- config 4: paged tree attention
-    B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
-    tm = SpeculativeDraftTree(C4["depth"], C4["branches"], "tree").tree_mask.numpy()
-    T = tm.shape[0]
-    g = torch.Generator(device=dev).manual_seed(3)
-    kp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
-    vp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
-    perm = torch.randperm(P, generator=torch.Generator().manual_seed(3))
-    per = ctx // ps
-    table = torch.stack([perm[b * per:(b + 1) * per].repeat_interleave(ps) for b in range(B)]).to(torch.int32)
-    tdev = table.to(dev)
-    q = torch.randn(B, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
-    tk = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
-    tv = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
-    tmd = torch.tensor(tm, device=dev)
-    atimes = []
-    for v in attn_variants:
-        N.set_attn_kernel(v)
-        atimes.append((v, time_call(lambda: mk.fused_tree_attention_paged(q, kp, vp, tdev, tk, tv, tmd), iters)))
-    pages0 = table[0].view(-1, ps)[:, 0].long()
-    kps, vps = f32(kp[pages0.to(dev)][:, 0:1]), f32(vp[pages0.to(dev)][:, 0:1])
-    tab0 = np.repeat(np.arange(pages0.numel(), dtype=np.int32), ps)[None, :]
-    q0, tk0, tv0 = f32(q[0:1]), f32(tk[0:1]), f32(tv[0:1])
-    ct = cpu_time(lambda: O.tree_attention_paged_fast(q0, kps, vps, tab0, ctx, ps, tk0, tv0, tm, 1 / math.sqrt(D)))
-    for v, t in atimes:
-        emit("config4_tree_attention", B * T, "tree-node queries/s", t, "hbm", C4_BYTES / t / 1e9, peaks["hbm"],
-             "measured hbm_gbs", T, ct, {"tflops": C4_FLOP / t / 1e12, "attn_kernel": v})
-    del kp, vp
-    # ---- config 5: fused_multi_verify, tp = 1
-    Bv, S, K, V = C5["B"], C5["S"], C5["K"], C5["V"]
-    g = torch.Generator(device=dev).manual_seed(4)
-    hid = torch.randn(Bv, S, K, generator=g, device=dev).to(torch.bfloat16)
-    lm = (0.02 * torch.randn(V, K, generator=g, device=dev)).to(torch.bfloat16)
-    dr = torch.randint(0, V, (Bv, S - 1), device=dev, dtype=torch.int32)
-    times = timed_gemm(lambda: mv.fused_multi_verify(hid, lm, dr))
-    hs, lms, ds = f32(hid[:2]), f32(lm), dr[:2].cpu().numpy()
-    ct = cpu_time(lambda: O.fused_multi_verify(hs, lms, None, ds))
-    for v, t in times:
-        emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16_sus"],
-             "measured bf16_tflops_sustained", 2 * S, ct, {"gemm_schedule": v})
-    del lm
+            emit("config3_fp8", M, "rows/s", t, "tensor", flop / t / 1e12, 2 * peaks["bf16_sus"],
+                 "2 x measured bf16_tflops_sustained (nominal fp8:bf16 ratio; fp8 not measured)", rows, ct,
+                 {"dtype": "e4m3", "gemm_schedule": v})
+        del x, xq, wq
 
-    # ---- the reference's own verify benchmark geometry (bench_optimizations.py:58-113):
-    # B=32, S=5, K=256, V=8192 with bias, fp32 (the CUDA-core exact-fp32 GEMM) and bf16
-    for dt in (torch.float32, torch.bfloat16):
-        g = torch.Generator(device=dev).manual_seed(0)
-        hr = torch.randn(32, 5, 256, generator=g, device=dev).to(dt)
-        wr = torch.randn(8192, 256, generator=g, device=dev).to(dt)
-        br = torch.randn(8192, generator=g, device=dev)
-        dr_ = torch.randint(0, 8192, (32, 4), generator=g, device=dev, dtype=torch.int32)
-        t = time_call(lambda: mv.fused_multi_verify(hr, wr, dr_, br), iters)
-        hs_, ws2, bs_, ds_ = f32(hr[:4]), f32(wr), f32(br), dr_[:4].cpu().numpy()
-        ct = cpu_time(lambda: O.fused_multi_verify(hs_, ws2, bs_, ds_))
-        flop = 2.0 * 32 * 5 * 256 * 8192
-        emit(f"ref_bench_fusion_verify_{'fp32' if dt == torch.float32 else 'bf16'}", 32 * 5,
-             "verified candidates/s", t, "tensor", flop / t / 1e12, peaks["bf16"],
-             "measured bf16_tflops (burst)", 4 * 5, ct,
-             {"dtype": "f32" if dt == torch.float32 else "bf16",
-              "note": "launch-bound size (0.34 GFLOP); the reference times it at bench_optimizations.py:58-113"})
-        del hr, wr
+    def sec_config4():
+        # ---- config 4: paged tree attention
+        B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
+        tm = SpeculativeDraftTree(C4["depth"], C4["branches"], "tree").tree_mask.numpy()
+        T = tm.shape[0]
+        g = torch.Generator(device=dev).manual_seed(3)
+        kp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
+        vp = torch.randn(P, B, Hkv, ps, D, generator=g, device=dev).to(torch.bfloat16)
+        perm = torch.randperm(P, generator=torch.Generator().manual_seed(3))
+        per = ctx // ps
+        table = torch.stack([perm[b * per:(b + 1) * per].repeat_interleave(ps) for b in range(B)]).to(torch.int32)
+        tdev = table.to(dev)
+        q = torch.randn(B, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+        tk = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+        tv = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+        tmd = torch.tensor(tm, device=dev)
+        atimes = []
+        for v in attn_variants:
+            N.set_attn_kernel(v)
+            atimes.append((v, time_call(lambda: mk.fused_tree_attention_paged(q, kp, vp, tdev, tk, tv, tmd), iters)))
+        pages0 = table[0].view(-1, ps)[:, 0].long()
+        kps, vps = f32(kp[pages0.to(dev)][:, 0:1]), f32(vp[pages0.to(dev)][:, 0:1])
+        tab0 = np.repeat(np.arange(pages0.numel(), dtype=np.int32), ps)[None, :]
+        q0, tk0, tv0 = f32(q[0:1]), f32(tk[0:1]), f32(tv[0:1])
+        ct = cpu_time(lambda: O.tree_attention_paged_fast(q0, kps, vps, tab0, ctx, ps, tk0, tv0, tm, 1 / math.sqrt(D)))
+        for v, t in atimes:
+            emit("config4_tree_attention", B * T, "tree-node queries/s", t, "hbm", C4_BYTES / t / 1e9, peaks["hbm"],
+                 "measured hbm_gbs", T, ct, {"tflops": C4_FLOP / t / 1e12, "attn_kernel": v})
+        del kp, vp
 
-    # ---- operators around the path (not BASELINE configs): one line each
-    # tree attention -> RMSNorm -> linear: the reference's own bench geometry
-    # (bench_memory.py:96, fp32) and a draft-head shape (bf16, D = hidden)
-    for (Bm, Hm, Dm, Lm, Nm, dt) in ((64, 4, 64, 32, 256, torch.float32),
-                                    (64, 1, 4096, 64, 32000, torch.bfloat16)):
-        g = torch.Generator(device=dev).manual_seed(5)
-        qm = torch.randn(Bm, Hm, Dm, generator=g, device=dev).to(dt)
-        km = torch.randn(Bm, Hm, Lm, Dm, generator=g, device=dev).to(dt)
-        vm = torch.randn(Bm, Hm, Lm, Dm, generator=g, device=dev).to(dt)
-        mm = (torch.rand(Lm, generator=g, device=dev) > 0.3).float()
-        rw = 1.0 + 0.1 * torch.randn(Dm, generator=g, device=dev)
-        pw = (0.05 * torch.randn(Nm, Dm, generator=g, device=dev)).to(dt)
-        t = time_call(lambda: mk.fused_tree_attn_rmsnorm_linear(qm, km, vm, mm, pw, rms_w=rw), iters)
-        eb = qm.element_size()
-        byts = (2 * Bm * Hm * Lm * Dm + 2 * Bm * Hm * Dm + Nm * Dm) * eb + Bm * Hm * Nm * eb
-        flop = 2.0 * Bm * Hm * Nm * Dm
-        qs, ks, vs, ws_, ms_, rws = f32(qm[:2]), f32(km[:2]), f32(vm[:2]), f32(pw), f32(mm), f32(rw)
-        ct = cpu_time(lambda: O.tree_attn_rmsnorm_linear(qs, ks, vs, ms_, rws, ws_, None, None,
-                                                         1 / math.sqrt(Dm), 1e-6))
-        emit(f"tree_attn_rmsnorm_linear_B{Bm}_H{Hm}_D{Dm}_L{Lm}_N{Nm}", Bm * Hm, "rows/s", t, "hbm",
-             byts / t / 1e9, peaks["hbm"], "measured hbm_gbs", 2 * Hm, ct,
-             {"dtype": "f32" if dt == torch.float32 else "bf16", "tflops": flop / t / 1e12})
-    # the reference's single-query operators (CUDA-core decode kernel): paged
-    # attention over a config-4-sized context, tree attention over 512 keys
-    Bd, Hd, Ld, Dd, psd = 16, 32, 4096, 128, 16
-    g = torch.Generator(device=dev).manual_seed(8)
-    Pd = Bd * Ld // psd // Bd + 1
-    kpd = torch.randn(Pd, Bd, Hd, psd, Dd, generator=g, device=dev).to(torch.bfloat16)
-    vpd = torch.randn(Pd, Bd, Hd, psd, Dd, generator=g, device=dev).to(torch.bfloat16)
-    tab = torch.stack([torch.randperm(Pd - 1, generator=torch.Generator().manual_seed(b))[: Ld // psd]
-                       .repeat_interleave(psd) for b in range(Bd)]).to(torch.int32)
-    qd = torch.randn(Bd, Hd, Dd, generator=g, device=dev).to(torch.bfloat16)
-    tabd = tab.to(dev)
-    decode_variants = (1, 2) if args.compare else (N.decode_kernel(),)
+    def sec_config5():
+        # ---- config 5: fused_multi_verify, tp = 1
+        Bv, S, K, V = C5["B"], C5["S"], C5["K"], C5["V"]
+        g = torch.Generator(device=dev).manual_seed(4)
+        hid = torch.randn(Bv, S, K, generator=g, device=dev).to(torch.bfloat16)
+        lm = (0.02 * torch.randn(V, K, generator=g, device=dev)).to(torch.bfloat16)
+        dr = torch.randint(0, V, (Bv, S - 1), device=dev, dtype=torch.int32)
+        times = timed_gemm(lambda: mv.fused_multi_verify(hid, lm, dr))
+        hs, lms, ds = f32(hid[:2]), f32(lm), dr[:2].cpu().numpy()
+        ct = cpu_time(lambda: O.fused_multi_verify(hs, lms, None, ds))
+        for v, t in times:
+            emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16_sus"],
+                 "measured bf16_tflops_sustained", 2 * S, ct, {"gemm_schedule": v})
+        del lm
 
-    def timed_decode(fn):
-        out = []
-        for v in decode_variants:
-            N.set_decode_kernel(v)
-            out.append((v, time_call(fn, iters)))
-        return out
+    def sec_ref_bench_fusion_verify():
+        # ---- the reference's own verify benchmark geometry (bench_optimizations.py:58-113):
+        # B=32, S=5, K=256, V=8192 with bias, fp32 (the CUDA-core exact-fp32 GEMM) and bf16
+        for dt in (torch.float32, torch.bfloat16):
+            g = torch.Generator(device=dev).manual_seed(0)
+            hr = torch.randn(32, 5, 256, generator=g, device=dev).to(dt)
+            wr = torch.randn(8192, 256, generator=g, device=dev).to(dt)
+            br = torch.randn(8192, generator=g, device=dev)
+            dr_ = torch.randint(0, 8192, (32, 4), generator=g, device=dev, dtype=torch.int32)
+            t = time_call(lambda: mv.fused_multi_verify(hr, wr, dr_, br), iters)
+            hs_, ws2, bs_, ds_ = f32(hr[:4]), f32(wr), f32(br), dr_[:4].cpu().numpy()
+            ct = cpu_time(lambda: O.fused_multi_verify(hs_, ws2, bs_, ds_))
+            flop = 2.0 * 32 * 5 * 256 * 8192
+            emit(f"ref_bench_fusion_verify_{'fp32' if dt == torch.float32 else 'bf16'}", 32 * 5,
+                 "verified candidates/s", t, "tensor", flop / t / 1e12, peaks["bf16"],
+                 "measured bf16_tflops (burst)", 4 * 5, ct,
+                 {"dtype": "f32" if dt == torch.float32 else "bf16",
+                  "note": "launch-bound size (0.34 GFLOP); the reference times it at bench_optimizations.py:58-113"})
+            del hr, wr
 
-    times = timed_decode(lambda: mk.fused_paged_attention(qd, kpd, vpd, tabd, psd))
-    byts = 2 * Bd * Hd * Ld * Dd * 2 + 2 * Bd * Hd * Dd * 2
-    kps_, vps_ = f32(kpd[:, 0:1]), f32(vpd[:, 0:1])
-    q1, tab1 = f32(qd[0:1]), tab[0:1].numpy()
-    ct = cpu_time(lambda: O.paged_attention(q1, kps_, vps_, tab1, psd, 1 / math.sqrt(Dd)))
-    for v, t in times:
-        emit("paged_attention_B16_H32_L4096_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9,
-             peaks["hbm"], "measured hbm_gbs", Hd, ct, {"decode_kernel": v})
-    del kpd, vpd
-    Lt = 512
-    kt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
-    vt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
-    mt = (torch.rand(Lt, generator=g, device=dev) > 0.2).float()
-    times = timed_decode(lambda: mk.fused_tree_attention(qd, kt, vt, mt))
-    byts = 2 * Bd * Hd * Lt * Dd * 2 + 2 * Bd * Hd * Dd * 2
-    kt1, vt1, mt1 = f32(kt[0:1]), f32(vt[0:1]), f32(mt)
-    ct = cpu_time(lambda: O.tree_attention(q1, kt1, vt1, mt1, 1 / math.sqrt(Dd)))
-    for v, t in times:
-        emit("tree_attention_B16_H32_L512_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9,
-             peaks["hbm"], "measured hbm_gbs", Hd, ct, {"decode_kernel": v})
-    del kt, vt
-    # INT4 weights, decode-sized M (streamed GEMV)
-    Mi, Ni, Ki, gi = 1, 14336, 4096, 128
-    g = torch.Generator(device=dev).manual_seed(6)
-    pk, sc = mk.quantize_int4(torch.randn(Ni, Ki, generator=g, device=dev), group=gi)
-    xi = torch.randn(Mi, Ki, generator=g, device=dev).to(torch.bfloat16)
-    t = time_call(lambda: mk.fused_int4_matmul(xi, pk, sc, Ki, gi), iters)
-    byts = Ni * Ki / 2 + sc.numel() * 4 + Mi * Ki * 2 + Mi * Ni * 2
-    pks, scs, xis = pk.cpu().numpy(), sc.cpu().numpy(), f32(xi)
-    ct = cpu_time(lambda: O.int4_matmul(xis, pks, scs, Ki, gi))
-    emit("int4_matmul_M1_N14336_K4096_g128", Mi, "rows/s", t, "hbm", byts / t / 1e9, peaks["hbm"],
-         "measured hbm_gbs", Mi, ct, {"dtype": "int4 x bf16"})
-    # FP8 KV-cache decode attention
-    Ba, Ha, La, Da = 16, 32, 4096, 128
-    g = torch.Generator(device=dev).manual_seed(7)
-    qa = torch.randn(Ba, Ha, Da, generator=g, device=dev).to(torch.bfloat16)
-    ka = torch.randn(Ba, Ha, La, Da, generator=g, device=dev).to(torch.float8_e4m3fn)
-    va = torch.randn(Ba, Ha, La, Da, generator=g, device=dev).to(torch.float8_e4m3fn)
-    ksa = torch.rand(Ha, generator=g, device=dev) + 0.5
-    vsa = torch.rand(Ha, generator=g, device=dev) + 0.5
-    t = time_call(lambda: mk.fused_causal_attention_fp8(qa, ka, va, ksa, vsa), iters)
-    byts = 2 * Ba * Ha * La * Da + 2 * 2 * Ba * Ha * Da
-    q0, k0 = f32(qa[:1]), O.e4m3_bits_to_f32(ka[:1].view(torch.uint8).cpu().numpy())
-    v0 = O.e4m3_bits_to_f32(va[:1].view(torch.uint8).cpu().numpy())
-    ks0, vs0 = f32(ksa), f32(vsa)
-    ct = cpu_time(lambda: O.causal_attention_scaled(q0, k0, v0, ks0, vs0, 1 / math.sqrt(Da)))
-    emit("causal_attention_fp8_B16_H32_L4096_D128", Ba * Ha, "query rows/s", t, "hbm", byts / t / 1e9,
-         peaks["hbm"], "measured hbm_gbs", Ha, ct, {"dtype": "e4m3 kv, bf16 q"})
+    def sec_operators():
+        # ---- operators around the path (not BASELINE configs): one line each
+        # tree attention -> RMSNorm -> linear: the reference's own bench geometry
+        # (bench_memory.py:96, fp32) and a draft-head shape (bf16, D = hidden)
+        for (Bm, Hm, Dm, Lm, Nm, dt) in ((64, 4, 64, 32, 256, torch.float32),
+                                        (64, 1, 4096, 64, 32000, torch.bfloat16)):
+            g = torch.Generator(device=dev).manual_seed(5)
+            qm = torch.randn(Bm, Hm, Dm, generator=g, device=dev).to(dt)
+            km = torch.randn(Bm, Hm, Lm, Dm, generator=g, device=dev).to(dt)
+            vm = torch.randn(Bm, Hm, Lm, Dm, generator=g, device=dev).to(dt)
+            mm = (torch.rand(Lm, generator=g, device=dev) > 0.3).float()
+            rw = 1.0 + 0.1 * torch.randn(Dm, generator=g, device=dev)
+            pw = (0.05 * torch.randn(Nm, Dm, generator=g, device=dev)).to(dt)
+            t = time_call(lambda: mk.fused_tree_attn_rmsnorm_linear(qm, km, vm, mm, pw, rms_w=rw), iters)
+            eb = qm.element_size()
+            byts = (2 * Bm * Hm * Lm * Dm + 2 * Bm * Hm * Dm + Nm * Dm) * eb + Bm * Hm * Nm * eb
+            flop = 2.0 * Bm * Hm * Nm * Dm
+            qs, ks, vs, ws_, ms_, rws = f32(qm[:2]), f32(km[:2]), f32(vm[:2]), f32(pw), f32(mm), f32(rw)
+            ct = cpu_time(lambda: O.tree_attn_rmsnorm_linear(qs, ks, vs, ms_, rws, ws_, None, None,
+                                                             1 / math.sqrt(Dm), 1e-6))
+            emit(f"tree_attn_rmsnorm_linear_B{Bm}_H{Hm}_D{Dm}_L{Lm}_N{Nm}", Bm * Hm, "rows/s", t, "hbm",
+                 byts / t / 1e9, peaks["hbm"], "measured hbm_gbs", 2 * Hm, ct,
+                 {"dtype": "f32" if dt == torch.float32 else "bf16", "tflops": flop / t / 1e12})
+        # the reference's single-query operators (CUDA-core decode kernel): paged
+        # attention over a config-4-sized context, tree attention over 512 keys
+        Bd, Hd, Ld, Dd, psd = 16, 32, 4096, 128, 16
+        g = torch.Generator(device=dev).manual_seed(8)
+        Pd = Bd * Ld // psd // Bd + 1
+        kpd = torch.randn(Pd, Bd, Hd, psd, Dd, generator=g, device=dev).to(torch.bfloat16)
+        vpd = torch.randn(Pd, Bd, Hd, psd, Dd, generator=g, device=dev).to(torch.bfloat16)
+        tab = torch.stack([torch.randperm(Pd - 1, generator=torch.Generator().manual_seed(b))[: Ld // psd]
+                           .repeat_interleave(psd) for b in range(Bd)]).to(torch.int32)
+        qd = torch.randn(Bd, Hd, Dd, generator=g, device=dev).to(torch.bfloat16)
+        tabd = tab.to(dev)
+        decode_variants = (1, 2) if args.compare else (N.decode_kernel(),)
+
+        def timed_decode(fn):
+            out = []
+            for v in decode_variants:
+                N.set_decode_kernel(v)
+                out.append((v, time_call(fn, iters)))
+            return out
+
+        times = timed_decode(lambda: mk.fused_paged_attention(qd, kpd, vpd, tabd, psd))
+        byts = 2 * Bd * Hd * Ld * Dd * 2 + 2 * Bd * Hd * Dd * 2
+        kps_, vps_ = f32(kpd[:, 0:1]), f32(vpd[:, 0:1])
+        q1, tab1 = f32(qd[0:1]), tab[0:1].numpy()
+        ct = cpu_time(lambda: O.paged_attention(q1, kps_, vps_, tab1, psd, 1 / math.sqrt(Dd)))
+        for v, t in times:
+            emit("paged_attention_B16_H32_L4096_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9,
+                 peaks["hbm"], "measured hbm_gbs", Hd, ct, {"decode_kernel": v})
+        del kpd, vpd
+        Lt = 512
+        kt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
+        vt = torch.randn(Bd, Hd, Lt, Dd, generator=g, device=dev).to(torch.bfloat16)
+        mt = (torch.rand(Lt, generator=g, device=dev) > 0.2).float()
+        times = timed_decode(lambda: mk.fused_tree_attention(qd, kt, vt, mt))
+        byts = 2 * Bd * Hd * Lt * Dd * 2 + 2 * Bd * Hd * Dd * 2
+        kt1, vt1, mt1 = f32(kt[0:1]), f32(vt[0:1]), f32(mt)
+        ct = cpu_time(lambda: O.tree_attention(q1, kt1, vt1, mt1, 1 / math.sqrt(Dd)))
+        for v, t in times:
+            emit("tree_attention_B16_H32_L512_D128", Bd * Hd, "query rows/s", t, "hbm", byts / t / 1e9,
+                 peaks["hbm"], "measured hbm_gbs", Hd, ct, {"decode_kernel": v})
+        del kt, vt
+        # INT4 weights, decode-sized M (streamed GEMV)
+        Mi, Ni, Ki, gi = 1, 14336, 4096, 128
+        g = torch.Generator(device=dev).manual_seed(6)
+        pk, sc = mk.quantize_int4(torch.randn(Ni, Ki, generator=g, device=dev), group=gi)
+        xi = torch.randn(Mi, Ki, generator=g, device=dev).to(torch.bfloat16)
+        t = time_call(lambda: mk.fused_int4_matmul(xi, pk, sc, Ki, gi), iters)
+        byts = Ni * Ki / 2 + sc.numel() * 4 + Mi * Ki * 2 + Mi * Ni * 2
+        pks, scs, xis = pk.cpu().numpy(), sc.cpu().numpy(), f32(xi)
+        ct = cpu_time(lambda: O.int4_matmul(xis, pks, scs, Ki, gi))
+        emit("int4_matmul_M1_N14336_K4096_g128", Mi, "rows/s", t, "hbm", byts / t / 1e9, peaks["hbm"],
+             "measured hbm_gbs", Mi, ct, {"dtype": "int4 x bf16"})
+        # FP8 KV-cache decode attention
+        Ba, Ha, La, Da = 16, 32, 4096, 128
+        g = torch.Generator(device=dev).manual_seed(7)
+        qa = torch.randn(Ba, Ha, Da, generator=g, device=dev).to(torch.bfloat16)
+        ka = torch.randn(Ba, Ha, La, Da, generator=g, device=dev).to(torch.float8_e4m3fn)
+        va = torch.randn(Ba, Ha, La, Da, generator=g, device=dev).to(torch.float8_e4m3fn)
+        ksa = torch.rand(Ha, generator=g, device=dev) + 0.5
+        vsa = torch.rand(Ha, generator=g, device=dev) + 0.5
+        t = time_call(lambda: mk.fused_causal_attention_fp8(qa, ka, va, ksa, vsa), iters)
+        byts = 2 * Ba * Ha * La * Da + 2 * 2 * Ba * Ha * Da
+        q0, k0 = f32(qa[:1]), O.e4m3_bits_to_f32(ka[:1].view(torch.uint8).cpu().numpy())
+        v0 = O.e4m3_bits_to_f32(va[:1].view(torch.uint8).cpu().numpy())
+        ks0, vs0 = f32(ksa), f32(vsa)
+        ct = cpu_time(lambda: O.causal_attention_scaled(q0, k0, v0, ks0, vs0, 1 / math.sqrt(Da)))
+        emit("causal_attention_fp8_B16_H32_L4096_D128", Ba * Ha, "query rows/s", t, "hbm", byts / t / 1e9,
+             peaks["hbm"], "measured hbm_gbs", Ha, ct, {"dtype": "e4m3 kv, bf16 q"})
+
+    sections = (("config1", sec_config1), ("config2", sec_config2), ("config3", sec_config3),
+                ("config4", sec_config4), ("config5", sec_config5),
+                ("ref_bench_fusion_verify", sec_ref_bench_fusion_verify), ("operators", sec_operators))
+    only = [p for p in (args.sweep_only or "").split(",") if p]
+    for name, section in sections:
+        if not only or any(name.startswith(p) for p in only):
+            section()
     assert N.device_status(dev) == 0
 
 
@@ -949,6 +967,10 @@ def main():
     ap.add_argument("--profile-case", choices=["verify", "rms", "attention"], default=None,
                     help="call one operator at its BASELINE config --steps times (the workload of the ncu "
                          "captures in profiles/)")
+    ap.add_argument("--sweep-only", default="",
+                    help="with --sweep: comma-separated section names to run (config1..config5, "
+                         "ref_bench_fusion_verify, operators; prefixes match), so sections can run in separate "
+                         "processes")
     ap.add_argument("--compare", action="store_true",
                     help="with --sweep: every GEMM config under both schedules, config 4 under both attention "
                          "kernels, the single-query lines under both decode kernels")
