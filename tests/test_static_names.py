@@ -176,3 +176,46 @@ def test_product_never_uses_the_oracle():
                 if "oracle" in src or "mtp_oracle" in src:
                     hits.append(os.path.relpath(os.path.join(root, f), REPO))
     assert hits == []
+
+
+def reads_before_assignment(path):
+    """Names a function reads on an earlier line than its first assignment
+    of them in its own body (an UnboundLocalError waiting for the call),
+    for every top-level and nested function; lambdas and comprehensions are
+    left to their own scopes."""
+    import ast
+    tree = ast.parse(open(os.path.join(REPO, path)).read())
+    out = []
+    scopes = (ast.FunctionDef, ast.AsyncFunctionDef, ast.Lambda, ast.ListComp, ast.GeneratorExp, ast.DictComp,
+              ast.SetComp, ast.ClassDef)
+
+    def check(fn):
+        assigned, reads = {}, []
+
+        def visit(node):
+            for ch in ast.iter_child_nodes(node):
+                if isinstance(ch, scopes):
+                    continue
+                if isinstance(ch, ast.Name):
+                    if isinstance(ch.ctx, ast.Store):
+                        assigned[ch.id] = min(assigned.get(ch.id, 10 ** 9), ch.lineno)
+                    elif isinstance(ch.ctx, ast.Load):
+                        reads.append((ch.id, ch.lineno))
+                visit(ch)
+
+        for arg in fn.args.args + fn.args.kwonlyargs:
+            assigned[arg.arg] = 0
+        visit(fn)
+        declared = {n for st in ast.walk(fn) if isinstance(st, (ast.Global, ast.Nonlocal)) for n in st.names}
+        out.extend(f"{path}:{l} {fn.name}: {n}" for n, l in sorted(set(reads))
+                   if n in assigned and l < assigned[n] and n not in declared)
+
+    for node in ast.walk(tree):
+        if isinstance(node, (ast.FunctionDef, ast.AsyncFunctionDef)):
+            check(node)
+    return out
+
+
+@pytest.mark.parametrize("path", [f for f in FILES if not f.startswith("tests/")])
+def test_no_read_before_assignment(path):
+    assert reads_before_assignment(path) == []
