@@ -42,6 +42,6 @@ def test_child(name):
     if kexpr:
         cmd += ["-k", kexpr]
     cmd += [os.path.join(HERE, f) for f in files]
-    r = subprocess.run(cmd, env=env, cwd=os.path.dirname(HERE), capture_output=True, text=True, timeout=1200)
+    r = subprocess.run(cmd, env=env, cwd=os.path.dirname(HERE), capture_output=True, text=True, timeout=600)
     tail = "\n".join((r.stdout + r.stderr).strip().splitlines()[-40:])
     assert r.returncode == 0, f"child pytest for {name} exited {r.returncode}:\n{tail}"
