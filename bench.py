@@ -9,9 +9,16 @@ A step is one pass of the hot path over the BASELINE workloads:
 and verifies B*S = 384 candidate tokens.  On N GPUs (torchrun, one rank per
 GPU) the same total work is split tensor-parallel: stage 1 by output
 columns, stage 2 by KV heads, stage 3 by vocabulary with one all-reduce(MAX)
-of packed (logit, index) keys over NCCL -- strong scaling.
+of packed (logit, index) keys over NCCL -- strong scaling.  With
+--scaling weak, every rank runs stages 1 and 2 whole on its own batch and
+stage 3 verifies every rank's sequences against its vocabulary block
+(candidates all-gathered, keys all-reduced) -- weak scaling.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--scaling strong|weak] [--exchange nccl|p2p|fused|abi]
+                    [--gemm-schedule dp|streamk] [--gemm-tile-rows 128|256]
+    python bench.py --sweep [--sweep-only SECTIONS] [--compare]   # one line per config
+    python bench.py --profile-case verify|rms|attention --steps K # the ncu capture workloads
 
 --impl reference times the reference's eager algorithm as restated by the CPU
 oracle (the reference is Python and cannot be shipped to the GPU box) on the
