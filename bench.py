@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Tree-verification forward step benchmark (one JSON line on rank 0).
 
-A step is one pass of the hot path over the BASELINE workloads:
+A step is one pass of the hot path over the benchmark workloads:
   1. fused RMSNorm -> linear, bf16, M=512 K=4096 N=14336 (config 2, gamma on)
   2. paged tree attention, bf16, B=16 Hq=32 Hkv=8 D=128 page 16, ctx 4096,
      64-node tree (config 4)
@@ -46,7 +46,7 @@ for _p in (REPO, PKG):
 METRIC = "verified tokens/sec (fused norm-linear+tree-attn+verify); % TC/HBM roofline"
 UNIT = "verified tokens/s"
 
-# BASELINE configs
+# benchmark configs
 C2 = dict(M=512, K=4096, N=14336, eps=1e-5)
 C4 = dict(B=16, Hq=32, Hkv=8, D=128, ps=16, ctx=4096, P=4096, depth=16, branches=4)
 C5 = dict(B=64, S=6, K=4096, V=128256)
@@ -459,7 +459,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: seeded N(0,1) activations / KV, random-init weights of the BASELINE shapes",
+        "data": "synthetic: seeded N(0,1) activations / KV, random-init weights of the benchmark shapes",
         "config": {"workload": WORKLOAD, "tokens_per_step": tokens_per_step, "global_batch": BG,
                    "seq_len": C5["S"],
                    "parallelism": "tp1" if world == 1 else
@@ -568,7 +568,7 @@ def run_reference(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
-        "data": "synthetic: seeded N(0,1) inputs of the BASELINE shapes (host)",
+        "data": "synthetic: seeded N(0,1) inputs of the benchmark shapes (host)",
         "config": {"workload": WORKLOAD, "tokens_per_step": TOKENS_PER_STEP, "global_batch": C5["B"],
                    "seq_len": C5["S"], "parallelism": "host cpu"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
@@ -581,7 +581,7 @@ def run_reference(args):
 
 
 def run_sweep(args):
-    """--sweep: every BASELINE config timed on its own (one JSON line each,
+    """--sweep: every benchmark config timed on its own (one JSON line each,
     marked "sweep"), 1 GPU.  L2 is flushed (256 MB write) between timed
     calls; each call is bracketed by CUDA events on its stream; the median is
     reported with its roofline fraction and a CPU-oracle baseline on a bounded
@@ -797,7 +797,7 @@ def run_sweep(args):
             del hr, wr
 
     def sec_operators():
-        # ---- operators around the path (not BASELINE configs): one line each
+        # ---- operators around the path (not benchmark configs): one line each
         # tree attention -> RMSNorm -> linear: the reference's own bench geometry
         # (bench_memory.py:96, fp32) and a draft-head shape (bf16, D = hidden)
         for (Bm, Hm, Dm, Lm, Nm, dt) in ((64, 4, 64, 32, 256, torch.float32),
@@ -899,7 +899,7 @@ def run_sweep(args):
 
 
 def run_profile_case(args):
-    """--profile-case: one operator at its BASELINE config, called --steps
+    """--profile-case: one operator at its benchmark config, called --steps
     times with CUDA-event timing printed per call -- the small, fixed
     workload the ncu captures in profiles/ are taken on."""
     import torch
@@ -963,7 +963,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch every call eagerly")
     ap.add_argument("--graph", action="store_true", help="also replay captured graphs when n_gpus > 1")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
-    ap.add_argument("--sweep", action="store_true", help="time every BASELINE config on its own (1 GPU)")
+    ap.add_argument("--sweep", action="store_true", help="time every benchmark config on its own (1 GPU)")
     ap.add_argument("--exchange", choices=["nccl", "p2p", "fused", "abi"], default="nccl",
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
                          "the all-reduce fused into the shard GEMM, or the one-call C-ABI verify over the "
@@ -972,7 +972,7 @@ def main():
                     help="N > 1: strong = the 1-GPU job split tensor-parallel; weak = configs 2 and 4 whole on "
                          "every GPU, the verify over every rank's sequences with the lm_head vocab-sharded")
     ap.add_argument("--profile-case", choices=["verify", "rms", "attention"], default=None,
-                    help="call one operator at its BASELINE config --steps times (the workload of the ncu "
+                    help="call one operator at its benchmark config --steps times (the workload of the ncu "
                          "captures in profiles/)")
     ap.add_argument("--sweep-only", default="",
                     help="with --sweep: comma-separated section names to run (config1..config5, "

@@ -1,7 +1,7 @@
 """Parity of the sm_100a kernels (through the drop-in modules and the C ABI)
 against the CPU oracle on the same seeded inputs.  GPU only.
 
-Tolerances (from the task's BASELINE):
+Tolerances (the benchmark specification's):
   * fp32 paths: max abs error <= 1e-4 (the reference's own bound,
     test_engine.py:5, mtp_engine.py:1644-1651);
   * bf16 GEMM outputs: ||y - ref||_inf / ||ref||_inf <= 2e-2 and
@@ -124,7 +124,7 @@ def test_verify_golden(mods, golden):
 
 
 def test_config1_chain(mods, golden):
-    """rmsnorm_linear (gamma) -> fused_multi_verify, fp32."""
+    """benchmark config 1: rmsnorm_linear (gamma) -> fused_multi_verify, fp32."""
     mk, mv, _ = mods
     g = golden("config1.npz")
     gen = torch.Generator().manual_seed(0)
@@ -184,7 +184,7 @@ def test_rmsnorm_linear_bf16_shapes(mods, M, N, K):
 
 
 def test_config2_rmsnorm_linear_bf16(mods):
-    """BASELINE config 2 (seed 1): M=512, K=4096, N=14336, gamma 1+N(0,0.1), eps 1e-5."""
+    """benchmark config 2 (seed 1): M=512, K=4096, N=14336, gamma 1+N(0,0.1), eps 1e-5."""
     mk, _, _ = mods
     M, K, N = 512, 4096, 14336
     g = torch.Generator(device=dev()).manual_seed(1)
@@ -198,7 +198,7 @@ def test_config2_rmsnorm_linear_bf16(mods):
 
 
 def test_config3_fp8(mods):
-    """BASELINE config 3 (seed 2): M=1024, K=8192, N=28672 e4m3, rows scaled to amax 448,
+    """benchmark config 3 (seed 2): M=1024, K=8192, N=28672 e4m3, rows scaled to amax 448,
     per-channel weight scales stored through pack_scales, bf16 out."""
     mk, _, _ = mods
     M, K, N = 1024, 8192, 28672
@@ -267,7 +267,7 @@ def test_multi_verify_bf16(mods, B, S, K, V, bias):
 
 
 def test_config5_verify_full(mods):
-    """BASELINE config 5 at tp=1 (seed 4): B=64, S=6, K=4096, V=128256 bf16, no bias."""
+    """benchmark config 5 at tp=1 (seed 4): B=64, S=6, K=4096, V=128256 bf16, no bias."""
     _, mv, mp = mods
     B, S, K, V = 64, 6, 4096, 128256
     g = torch.Generator(device=dev()).manual_seed(4)
@@ -324,7 +324,7 @@ def test_fused_verify_single_bf16(mods):
 
 
 def test_config4_tree_attention_paged(mods):
-    """BASELINE config 4 (seed 3): B=16, Hq=32, Hkv=8, D=128, page 16, ctx 4096 over a
+    """benchmark config 4 (seed 3): B=16, Hq=32, Hkv=8, D=128, page 16, ctx 4096 over a
     randomly permuted 4096-page pool, 64-node tree (depth 16, 4 branches), bf16."""
     mk, _, _ = mods
     B, Hq, Hkv, D, ps, ctx, P = 16, 32, 8, 128, 16, 4096, 4096

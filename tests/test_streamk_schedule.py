@@ -25,7 +25,7 @@ def check(M, Nn, K, dt=N.DT_BF16, sms=SMS, grid=0):
     assert st == 0, N.lib().mtp_last_error().decode()
 
 
-# BASELINE workloads (one GPU, and one rank of 8) plus shapes that cut tiles
+# benchmark workloads (one GPU, and one rank of 8) plus shapes that cut tiles
 # into many parts, leave CTAs without work, or have a single K block
 SHAPES = [
     (384, 128256, 4096, N.DT_BF16),   # config 5 verify, 1 GPU
