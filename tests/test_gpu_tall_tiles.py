@@ -119,3 +119,35 @@ def test_switch_roundtrip(N):
         N.set_gemm_tile_rows(m)
         assert L.mtp_gemm_tile_rows() == m
     assert L.mtp_set_gemm_tile_rows(3) == 8  # MTP_ERR_ARG
+
+
+def test_config5_verify_and_config2_shapes(N):
+    """At the benchmark sizes the cost model sends to 256-row tiles (mode 1):
+    the 1-GPU verify (384 x 128256 x 4096, a half row tile) must give the
+    128-row tiles' tokens exactly, and config 2 (512 x 14336 x 4096) the
+    same outputs within the bf16 bound."""
+    import mtp_fused_verify as mv
+    import mtp_kernels as mk
+    d = torch.device("cuda", 0)
+    g = torch.Generator(device=d).manual_seed(4)
+    hid = torch.randn(64, 6, 4096, generator=g, device=d).to(torch.bfloat16)
+    lm = (0.02 * torch.randn(128256, 4096, generator=g, device=d)).to(torch.bfloat16)
+    draft = torch.randint(0, 128256, (64, 5), generator=g, device=d, dtype=torch.int32)
+    N.set_gemm_tile_rows(0)
+    ref = mv.fused_multi_verify(hid, lm, draft)
+    N.set_gemm_tile_rows(1)
+    got = mv.fused_multi_verify(hid, lm, draft)
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    del lm
+    x = torch.randn(512, 4096, generator=g, device=d).to(torch.bfloat16)
+    W = (0.02 * torch.randn(14336, 4096, generator=g, device=d)).to(torch.bfloat16)
+    gam = 1.0 + 0.1 * torch.randn(4096, generator=g, device=d)
+    N.set_gemm_tile_rows(0)
+    y0 = mk.fused_rmsnorm_linear(x, W, None, 1e-5, norm_weight=gam)
+    N.set_gemm_tile_rows(1)
+    y1 = mk.fused_rmsnorm_linear(x, W, None, 1e-5, norm_weight=gam)
+    torch.cuda.synchronize()
+    assert (y1.float() - y0.float()).abs().max().item() <= 2e-2 * y0.float().abs().max().item()
+    assert N.device_status(d) == 0
