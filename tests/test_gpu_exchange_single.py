@@ -165,3 +165,32 @@ def test_fused_exchange_missing_peer_times_out(mods):
     ref = mv.fused_multi_verify(hid, w, draft)
     torch.cuda.synchronize()
     assert N.device_status(dev) == 0 and int(ref[1].min()) >= 0
+
+
+def test_fused_exchange_streamk_single_rank(mods):
+    """The fused GEMM+exchange under the stream-K schedule at the shape of
+    one rank of an 8-way verify (384 x 16032 x 4096, where the cost model
+    takes stream-K).  Integer-valued operands keep every split-K sum exact,
+    so the outputs must equal the data-parallel schedule's bit for bit,
+    ties included (lowest index)."""
+    N, mv = mods
+    d = torch.device("cuda", 0)
+    g = torch.Generator(device=d).manual_seed(5)
+    B, S, K, V = 64, 6, 4096, 16032
+    hid = torch.randint(-2, 3, (B, S, K), generator=g, device=d).to(torch.bfloat16)
+    w = torch.randint(-2, 3, (V, K), generator=g, device=d).to(torch.bfloat16)
+    draft = torch.randint(0, V, (B, S - 1), generator=g, device=d, dtype=torch.int32)
+    before = N.gemm_schedule()
+    try:
+        N.set_gemm_schedule(0)
+        ref = mv.fused_multi_verify(hid, w, draft)
+        N.set_gemm_schedule(1)
+        bufs, peers = fused_buffers(N, B * S, 1, 1)
+        for _ in range(2):
+            got = shard_fused(N, hid, w, draft, peers, 0, 1)
+            torch.cuda.synchronize()
+            for a, b in zip(got, ref):
+                assert torch.equal(a, b)
+    finally:
+        N.set_gemm_schedule(before)
+    assert N.device_status(d) == 0
