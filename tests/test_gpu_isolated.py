@@ -24,6 +24,7 @@ CHILDREN = {
     "tree_attn_rmsnorm_linear": (["test_gpu_tree_attn_rmsnorm_linear.py"], {}, None),
     "nccl_abi": (["test_gpu_nccl_abi.py"], {"NCCL_NVLS_ENABLE": "0"}, None),
     "exchange_single_gpu": (["test_gpu_exchange_single.py"], {}, None),
+    "edge_shapes": (["test_gpu_edge_shapes.py"], {}, None),
     "attention_64key_kernel": (["test_gpu_attention_tc.py", "test_gpu_parity.py"], {"MTP_ATTN_KERNEL": "2"},
                                "attention or edge_cases or device_status"),
     # smaller operators and whole-path checks, one child for all of them
