@@ -114,3 +114,41 @@ def test_tree_attention_paged_shapes(mods, B, Hq, Hkv, ps, ctx, depth, br):
                                  1.0 / math.sqrt(D))
     assert rel_err(np32(out), ref) <= REL_TOL
     assert N.device_status(dev()) == 0
+
+
+@pytest.mark.parametrize("M,N,K,bias", [(1, 300, 512, True), (70, 1000, 256, False), (256, 520, 4096, True)])
+def test_rmsnorm_linear_fp8_shapes(mods, M, N, K, bias):
+    """E4M3 weight with per-channel scales, activations quantised per token
+    in the row pre-pass: against the oracle on the dequantised operands
+    (the activation codes are recomputed from x as the kernel does)."""
+    _, mk, _, _ = mods
+    g = torch.Generator(device=dev()).manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g, device=dev()).to(torch.bfloat16)
+    wq, sw = mk.quantize_fp8_rows(0.05 * torch.randn(N, K, generator=g, device=dev()))
+    b = (0.1 * torch.randn(N, generator=g, device=dev())).to(torch.bfloat16) if bias else None
+    y = mk.fused_rmsnorm_linear_fp8(x, wq, sw, b, 1e-6)
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    xq, sx = mk.quantize_fp8_rows(x)
+    rows = list(range(min(M, 6)))
+    xd = O.e4m3_bits_to_f32(xq[rows].view(torch.uint8).cpu().numpy()) * np32(sx)[rows, None]
+    wd = O.e4m3_bits_to_f32(wq.view(torch.uint8).cpu().numpy())
+    ref = O.rmsnorm_linear_fp8(xd, wd, np32(sw), np32(b) if bias else None, 1e-6)
+    assert rel_err(np32(y[rows]), ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("B,H,L,D,dt", [(2, 3, 1, 72, torch.bfloat16), (1, 2, 300, 200, torch.float16),
+                                        (4, 1, 2049, 256, torch.bfloat16), (2, 2, 17, 40, torch.float32)])
+def test_single_query_tree_attention_shapes(mods, B, H, L, D, dt):
+    """fused_tree_attention (default single-query kernel) for head sizes
+    that are not powers of two, one key, fp32, and a context past 2048."""
+    N, mk, _, _ = mods
+    g = torch.Generator(device=dev()).manual_seed(B + H + L + D)
+    q = torch.randn(B, H, D, generator=g, device=dev()).to(dt)
+    k = torch.randn(B, H, L, D, generator=g, device=dev()).to(dt)
+    v = torch.randn(B, H, L, D, generator=g, device=dev()).to(dt)
+    mask = (torch.rand(L, generator=g, device=dev()) < 0.8).float()
+    mask[0] = 1.0
+    out = mk.fused_tree_attention(q, k, v, mask)
+    ref = O.tree_attention(np32(q), np32(k), np32(v), np32(mask), 1.0 / math.sqrt(D))
+    assert rel_err(np32(out), ref) <= (1e-4 if dt == torch.float32 else REL_TOL)
+    assert N.device_status(dev()) == 0
