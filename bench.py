@@ -387,6 +387,43 @@ def run_ours(args):
     for _ in range(max(1, args.warmup)):
         e2e_step()
     barrier()
+
+    # --e2e-graph (1 GPU): the same step -- uploads on the copy stream, the
+    # three stages, the read-back -- captured once as one graph; a step is
+    # then one replay and the host's wait for its result
+    e2e_graph = None
+    if args.e2e_graph and world == 1:
+        stage_fns = {0: lambda: stage1(d_x), 1: lambda: stage2(d_q, d_tk, d_tv), 2: lambda: stage3(d_hid, d_dr)}
+        e2e_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(e2e_graph, stream=stream):
+            copy_stream.wait_stream(stream)
+            with torch.cuda.stream(copy_stream):
+                for j in order:
+                    for h, d_ in groups[j]:
+                        d_.copy_(h, non_blocking=True)
+                    ready[j].record(copy_stream)
+            for j in order:
+                stream.wait_event(ready[j])
+                out = stage_fns[j]()
+                if j == 2:
+                    a, n_, c = out
+                    verified.record(stream)
+                    d2h_stream.wait_event(verified)
+                    with torch.cuda.stream(d2h_stream):
+                        o_acc.copy_(a, non_blocking=True)
+                        o_n.copy_(n_, non_blocking=True)
+                        o_c.copy_(c, non_blocking=True)
+            stream.wait_stream(copy_stream)
+            stream.wait_stream(d2h_stream)
+        stream.synchronize()
+
+        def e2e_step():  # noqa: F811 -- the graph form of the step above
+            with torch.cuda.stream(stream):
+                e2e_graph.replay()
+            stream.synchronize()
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -404,6 +441,7 @@ def run_ours(args):
     # graphs that hold NCCL calls must be gone before destroy_process_group:
     # drop every reference (the list and the replay closures), then collect
     run = None
+    e2e_graph = None
     graphs.clear()
     mp._EXCHANGES.clear()  # symmetric-memory buffers go before the process group too
     import gc
@@ -472,7 +510,8 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "order": "verify, RMSNorm-linear, attention; later uploads overlap earlier stages; host waits "
-                         "for each step's result"},
+                         "for each step's result",
+                "one_graph_per_step": bool(args.e2e_graph and world == 1)},
         "gpu_launches": launches,
         "clocks": clocks,
         "kernels": kernels,
@@ -968,6 +1007,8 @@ def main():
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
                          "the all-reduce fused into the shard GEMM, or the one-call C-ABI verify over the "
                          "library's own NCCL communicator")
+    ap.add_argument("--e2e-graph", action="store_true",
+                    help="1 GPU: capture the end-to-end step (uploads, stages, read-back) as one CUDA graph")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="N > 1: strong = the 1-GPU job split tensor-parallel; weak = configs 2 and 4 whole on "
                          "every GPU, the verify over every rank's sequences with the lm_head vocab-sharded")
