@@ -16,7 +16,12 @@
  *   - the return value is an MTP_* status; mtp_last_error() gives a
  *     thread-local message for the last non-zero status.
  *
- * Device-side checks (page ids out of range, inconsistent page tables,
+ * Page ids index the pool the way the reference's torch indexing does: an id
+ * in [-num_pages, num_pages) is valid and a negative one counts from the end
+ * (the -1 that PagedKVCache leaves in unreserved columns reads page
+ * num_pages - 1, mtp_engine.py:550-552, 582-586; mtp_kernels.py:839-848).
+ *
+ * Device-side checks (page ids outside [-num_pages, num_pages),
  * bounded waits that ran out) are recorded in a per-device error word that
  * mtp_device_status() reads.
  */
@@ -58,7 +63,21 @@ const char* mtp_last_error(void);
 
 /* Synchronises `stream`, then reports the current device's error word
  * (0 = clean, else an MTP_ERR_* code recorded by a kernel) in *code_out.
- * clear != 0 resets the word.  Returns MTP_OK or MTP_ERR_CUDA. */
+ * clear != 0 resets the word.  Returns MTP_OK or MTP_ERR_CUDA.
+ *
+ * After MTP_ERR_TIMEOUT (a bounded wait ran out; the call's outputs are
+ * undefined):
+ *   - single-device verify calls (mtp_fused_verify, mtp_fused_multi_verify,
+ *     mtp_verify_shard_keys*, mtp_fused_multi_verify_noalloc) still leave
+ *     their keys and ticket at rest, so the next call on the same workspace
+ *     runs normally; a workspace with GEMM schedule 1 (stream-K) room must
+ *     be filled again with mtp_keys_fill;
+ *   - the peer-memory exchanges (mtp_verify_exchange_chain,
+ *     mtp_verify_shard_fused) must be rebuilt on EVERY rank, not only on the
+ *     one that saw the timeout: synchronise all ranks, zero the exchange
+ *     buffers and epoch counters (mtp_verify_fused_init for the fused
+ *     form), then resume -- a rank that gave up is one call out of step
+ *     with its peers. */
 int mtp_device_status(void* stream, int* code_out, int clear);
 
 /* ------------------------------------------------------------------------- */
@@ -232,7 +251,7 @@ int mtp_int4_matmul(const void* x, int x_dtype, const uint8_t* packed, const flo
  * _eager_paged_attention, 832-856).  k_pages/v_pages:
  * [num_pages, B, H, page_size, D] (PagedKVCache layout, mtp_engine.py:542-549);
  * page_table: [B, L] int32, token t of sequence b at
- * pages[page_table[b,t], b, h, t % page_size]. */
+ * pages[page_table[b,t], b, h, t % page_size] (per token; any table). */
 int mtp_paged_attention(const void* q, const void* k_pages, const void* v_pages,
                         const int32_t* page_table, void* out, int dtype, int64_t B, int64_t H,
                         int64_t L, int64_t D, int64_t num_pages, int64_t page_size, float scale,
@@ -251,7 +270,11 @@ size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int6
  * `table_stride` >= ctx_len) followed by the tree nodes m with
  * tree_mask[n,m] > 0.5 (SpeculativeDraftTree.tree_mask,
  * mtp_engine.py:671-680).  q/out: [B,T,Hq,D]; tree_k/tree_v: [B,Hkv,T,D];
- * tree_mask: [T,T] float32. */
+ * tree_mask: [T,T] float32.  Any per-token page table is taken: 128-key
+ * chunks whose tokens fill whole pages are loaded page by page, others
+ * (tables that PagedKVCache.reserve built from token counts that are not
+ * multiples of page_size, or that swap_logical_pages rearranged,
+ * mtp_engine.py:567-593) token by token. */
 int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_pages,
                              const int32_t* page_table, int64_t table_stride, int64_t ctx_len,
                              const void* tree_k, const void* tree_v, const float* tree_mask,
@@ -290,8 +313,9 @@ int mtp_tree_attn_rmsnorm_linear(const void* q, const void* k, const void* v, in
  * node = node_idx[b, t] (e.g. the accepted path of a draft tree; NULL: t);
  * v likewise.  Pools [num_pages, B, H, page_size, D] in dtype; sources
  * [B, H, src_len, D] in src_dtype (converted like .to(dtype)); page_table
- * [B, table_stride] int32.  Rows whose page id or node index is out of range
- * are skipped and recorded (MTP_ERR_DEVICE via mtp_device_status). */
+ * [B, table_stride] int32.  Rows whose page id is outside [-num_pages,
+ * num_pages) or whose node index is out of range are skipped and recorded
+ * (MTP_ERR_DEVICE via mtp_device_status). */
 int mtp_paged_kv_write(void* k_pages, void* v_pages, int dtype, const int32_t* page_table, int64_t table_stride,
                        int64_t num_pages, int64_t page_size, const void* src_k, const void* src_v, int src_dtype,
                        int64_t src_len, const int32_t* node_idx, const int32_t* count, int64_t B, int64_t H,
@@ -432,7 +456,9 @@ int mtp_vocab_parallel_multi_verify(const void* hidden, int h_dtype, const void*
  * MTP_ERR_SHAPE.  The first call on a device looks up that array's device
  * address (make that first call before any stream capture).  Each call
  * clears the array first; all calls on a device share it, so calls whose
- * kernels overlap on the GPU (different streams, no ordering) race. */
+ * kernels overlap on the GPU (different streams, no ordering) race.  It
+ * runs the data-parallel GEMM schedule whatever mtp_set_gemm_schedule chose
+ * (the fixed array has no room for stream-K partials). */
 int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* weight, int w_dtype,
                                    const void* bias, int bias_dtype, const int32_t* draft, int8_t* accept,
                                    int32_t* accepted_n, int32_t* corrected, int64_t B, int64_t S, int64_t K,
@@ -484,7 +510,8 @@ int mtp_verify_shard_fused(const void* hidden, int h_dtype, const void* weight_s
  * generate_optimized (mtp_engine.py:1244-1258, 1326-1337), on the device so
  * the loop needs no .item(): n = min_b accepted_n[b] (one rollback index per
  * step); step_tokens[b, 0:width] = draft[b, 0:n] ++ corrected[b] when n < D
- * (width n + 1), else draft[b, 0:D] (width D); info[0] = n, info[1] = width.
+ * (width n + 1), else draft[b, 0:D] (width D); columns width .. D of each
+ * row (those below ld) are set to -1, "no token".  info[0] = n, info[1] = width.
  * draft [B,D], accepted_n/corrected [B] int32 (outputs of
  * mtp_fused_multi_verify), step_tokens [B, ld] int32 with ld >= D + 1
  * recommended (ld >= D accepted), info [2] int32.  One small launch. */

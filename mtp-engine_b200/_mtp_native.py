@@ -302,11 +302,41 @@ def verify_workspace(device: torch.device, rows: int, N: int = 0, K: int = 0, ab
     return workspace(device, "verify", need, _init)
 
 
+MTP_ERR_TIMEOUT = 5
+_timeout_hooks = []
+
+
+def on_timeout(fn) -> None:
+    """Register fn(device), called when device_status() reports that a
+    bounded wait ran out on `device` (mtp_parallel invalidates its peer
+    exchanges this way)."""
+    _timeout_hooks.append(fn)
+
+
+def _reset_after_timeout(device: torch.device) -> None:
+    """A kernel on `device` gave up on a bounded wait: drop every cached
+    workspace of the device, so the next call allocates it again and fills
+    it at rest (the stream-K counters of schedule 1 may have been left
+    mid-count), then tell the registered owners of other device state."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        for key in [k for k in _ws if k[0] == idx]:
+            del _ws[key]
+    for fn in list(_timeout_hooks):
+        fn(device)
+
+
 def device_status(device: torch.device, clear: bool = True) -> int:
+    """Synchronise the current stream of `device` and return its error word
+    (0 = clean, else an MTP_ERR_* code a kernel recorded).  On
+    MTP_ERR_TIMEOUT the device's cached workspaces are dropped, so later
+    calls start from workspaces at rest."""
     code = ctypes.c_int(0)
     with torch.cuda.device(device):
         check(lib().mtp_device_status(stream_handle(device), ctypes.byref(code), int(clear)),
               "mtp_device_status")
+    if code.value == MTP_ERR_TIMEOUT:
+        _reset_after_timeout(device)
     return code.value
 
 

@@ -1272,6 +1272,8 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
   attn::Params p{};
   p.page_table = page_table;
   p.table_stride = table_stride;
+  p.k_pool = static_cast<const uint8_t*>(k_pages);
+  p.v_pool = static_cast<const uint8_t*>(v_pages);
   p.tree_mask = tree_mask;
   p.out = out;
   p.B = (int)B;
@@ -1477,6 +1479,7 @@ int mtp_fused_multi_verify(const void* hidden, int h_dtype, const void* weight, 
   MTP_NVTX("mtp_fused_multi_verify");
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1 (S == D + 1), got S=%lld", (long long)S);
   if (B == 0) return MTP_OK;
+  if (B > INT64_MAX / S) return fail(MTP_ERR_SHAPE, "B*S overflows (B=%lld S=%lld)", (long long)B, (long long)S);
   if ((S > 1 && (!draft || !accept)) || !accepted_n || !corrected) return fail(MTP_ERR_ARG, "null output pointer");
   GemmEpilogue ep{};
   ep.finalize = FIN_CHAIN;
@@ -1499,10 +1502,10 @@ int mtp_fused_multi_verify_noalloc(const void* hidden, int h_dtype, const void* 
   MTP_NVTX("mtp_fused_multi_verify_noalloc");
   if (B < 0 || S < 1) return fail(MTP_ERR_SHAPE, "expected S >= 1 (S == D + 1), got S=%lld", (long long)S);
   if (B == 0) return MTP_OK;
+  if (B > MTP_NOALLOC_MAX_ROWS / S)  // checked before B * S is formed, so it cannot overflow
+    return fail(MTP_ERR_SHAPE, "B=%lld S=%lld: B*S exceeds the %d rows of the no-allocation scratch; use "
+                "mtp_fused_multi_verify", (long long)B, (long long)S, MTP_NOALLOC_MAX_ROWS);
   const int64_t rows = B * S;
-  if (rows > MTP_NOALLOC_MAX_ROWS)
-    return fail(MTP_ERR_SHAPE, "B*S=%lld exceeds the %d rows of the no-allocation scratch; use mtp_fused_multi_verify",
-                (long long)rows, MTP_NOALLOC_MAX_ROWS);
   if (int st = check_dims(rows, V, K)) return st;
   if (V == 0) return fail(MTP_ERR_SHAPE, "empty vocabulary");
   if (!valid_dtype(h_dtype) || !valid_dtype(w_dtype) || h_dtype == MTP_DTYPE_E4M3 || w_dtype == MTP_DTYPE_E4M3)

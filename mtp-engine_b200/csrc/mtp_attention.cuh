@@ -90,8 +90,8 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(AttnArgs a) {
       kp = a.k;
       vp = a.v;
     } else if (a.kind == ATTN_PAGED || j < a.ctx_len) {
-      const int32_t page = a.page_table[b * a.table_stride + j];
-      if (page < 0 || page >= a.num_pages) {
+      const int64_t page = resolve_page(a.page_table[b * a.table_stride + j], a.num_pages);
+      if (page < 0) {
         if (lane == 0) record_error(MTP_ERR_DEVICE);
         continue;
       }

@@ -28,8 +28,10 @@
 //               lazy rescaling (O in TMEM is rescaled only when the max
 //               grows by more than 2^8), exp2, P packed to bf16 pairs and
 //               stored back into TMEM with tcgen05.st.
-//   warp 10     page-table reader: checks and stages the page ids of up to
-//               16 chunks ahead of the TMA producer (shared-memory ring).
+//   warp 10     page-table reader: stages the page ids of up to 16 chunks
+//               ahead of the TMA producer (shared-memory ring) and marks
+//               chunks whose table is not page-granular, which the producer
+//               then gathers token by token (16-byte loads into the ring).
 // Long contexts with few units are split over CTAs (flash-decoding); the
 // partial (O, max, sum) triples are merged by attn_merge_kernel.
 // Every wait is bounded (mbar_wait).  No clusters; every TMA load fills its own CTA.
@@ -76,6 +78,8 @@ static __device__ unsigned long long g_attn_trace[8 * 2 * 64];
 struct Params {
   const int32_t* page_table;
   int64_t table_stride;
+  const uint8_t* k_pool;   // [P, B, Hkv, page_size, D] pools, for the per-token gather
+  const uint8_t* v_pool;
   const float* tree_mask;  // [T, T]
   void* out;               // [B, T, Hq, D]
   float* part_o;           // [units, splits, 256, D]   (splits > 1)
@@ -125,6 +129,52 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi, int dtype) {
   }
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Per-token gather of a context chunk (tables that are not page-granular).
+// rows[i] (lane l) = pool row -- ((page * B + b) * Hkv + h) * page_size + slot,
+// 256 bytes of K or V -- of token tok0 + l + 32 i, or -1 past the context or
+// for a page id outside [-P, P) (recorded as MTP_ERR_DEVICE, where the
+// reference raises); such rows are zero-filled, so masked keys stay finite.
+__device__ __forceinline__ void token_rows(const Params& p, int b, int kvh, int tok0, int lane, int (&rows)[4]) {
+  const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int tok = tok0 + lane + 32 * i;
+    rows[i] = -1;
+    if (tok < p.ctx_len) {
+      const int64_t pg = resolve_page(__ldg(table + tok), p.num_pages);
+      if (pg >= 0)
+        rows[i] = (int)(((pg * p.B + b) * p.Hkv + kvh) * p.ps + tok % p.ps);
+      else
+        record_error(MTP_ERR_DEVICE);
+    }
+  }
+}
+
+// Fills one 32 KB K or V buffer (128 keys x D = 128, two 16 KB halves of
+// 64 dims, rows 128 bytes, 128-byte swizzle: 16-byte piece j of row r sits
+// at piece j ^ (r & 7)) from the pool rows of token_rows.  Per step the warp
+// moves two tokens (lane l: piece l & 15 of token 2k + (l >> 4)), 16 loads
+// in flight per lane.
+__device__ __forceinline__ void fill_tokens(uint8_t* dst, const uint8_t* pool, const int (&rows)[4], int lane) {
+  const int j = lane & 15, half = j >> 3, jj = j & 7;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {  // tokens 32 q .. 32 q + 31, whose rows lane (i & 31) holds in rows[q]
+    uint4 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int i = 32 * q + 2 * u + (lane >> 4);
+      const int row = __shfl_sync(0xffffffffu, rows[q], i & 31);
+      v[u] = row >= 0 ? __ldg(reinterpret_cast<const uint4*>(pool + (int64_t)row * (kD * 2)) + j)
+                      : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int i = 32 * q + 2 * u + (lane >> 4);
+      *reinterpret_cast<uint4*>(dst + half * kHalfBytes + i * 128 + ((jj ^ (i & 7)) << 4)) = v[u];
+    }
+  }
 }
 
 // AB_FMT: 1 = bf16, 0 = f16 (q/k/v dtype)
@@ -212,20 +262,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool is_ctx = c < p.n_ctx_chunks;
       const int slot = (c - c0) % kIdRing;
       int pg = 0;
+      bool per_token = false;  // this chunk's table is not page-granular: gather token by token
+      int rows[4];             // per-token mode: pool row of token lane + 32 i (-1: zero-fill)
       if (is_ctx) {
         bool got = true;
         if (lane == 0) got = mbar_wait(&ids_full[slot], ((c - c0) / kIdRing) & 1, abort_flag);
         if (!__shfl_sync(0xffffffffu, got, 0)) break;
         if (lane < ppc) pg = sIds[slot * kMaxPagesPerChunk + lane];
+        per_token = sIds[slot * kMaxPagesPerChunk] < 0;
         __syncwarp();
         if (lane == 0) mbar_arrive(&ids_empty[slot]);
+        if (per_token) token_rows(p, b, kvh, c * kChunk, lane, rows);
       }
       for (int kv = 0; kv < 2; ++kv, ++item) {
         const int buf = item % kNumBuf;
         bool got = true;
         if (lane == 0) {
           got = mbar_wait(&buf_empty[buf], ((item / kNumBuf) & 1) ^ 1u, abort_flag);
-          if (got) mbar_expect_tx(&buf_full[buf], kTileBytes);
+          if (got && !per_token) mbar_expect_tx(&buf_full[buf], kTileBytes);
         }
         if (!__shfl_sync(0xffffffffu, got, 0)) {
           ok = false;
@@ -234,7 +288,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         ATTN_TRACE_IF(lane == 0, 6 + kv, 0, c - c0);
         __syncwarp();
         uint8_t* dst = sBuf + buf * kTileBytes;
-        if (is_ctx) {
+        if (per_token) {
+          // generic-proxy stores, made visible to the tensor cores (async
+          // proxy) by each lane's fence before the arrival
+          fill_tokens(dst, kv ? p.v_pool : p.k_pool, rows, lane);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&buf_full[buf]);
+        } else if (is_ctx) {
           if (lane < ppc) {
             const CUtensorMap* map = kv ? &tmV : &tmK;
             const int row = ((pg * p.B + b) * p.Hkv + kvh) * p.ps;
@@ -251,12 +312,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (n_iter > 0 && warp == 10) {
     // ---------------------------------------------------------------- page-table warp
-    // Reads and checks the page ids of up to kIdRing context chunks ahead of
-    // the TMA producer: lane i < pages_per_chunk takes page slot i, checks
-    // that every token of the page maps to the same in-range page (the
-    // reference gathers per token, mtp_kernels.py:520-531; whole-page loads
-    // are only equivalent when the table is page-granular, as PagedKVCache
-    // builds it) and records MTP_ERR_DEVICE otherwise.
+    // Reads the page ids of up to kIdRing context chunks ahead of the TMA
+    // producer and decides how each chunk is gathered.  The reference
+    // gathers per token (mtp_kernels.py:520-531, eager 839-848): key t of
+    // sequence b is slot t % page_size of page table[b, t].  Lane i <
+    // pages_per_chunk takes page slot i; when every token of every slot maps
+    // to its slot's page (resolved like torch indexing, resolve_page), the
+    // chunk is page-granular and the producer loads whole page slabs with
+    // TMA.  Otherwise -- tables that PagedKVCache.reserve built with
+    // n_tokens not a multiple of page_size, or that swap_logical_pages
+    // rearranged (mtp_engine.py:567-593) -- the chunk is marked per-token
+    // (page id -1 in slot 0) and the producer gathers it token by token.
     const int ppc = kChunk / p.ps;
     const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
     const int c_end = min(c1, p.n_ctx_chunks);
@@ -266,29 +332,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) got = mbar_wait(&ids_empty[slot], (((c - c0) / kIdRing) & 1) ^ 1u, abort_flag);
       if (!__shfl_sync(0xffffffffu, got, 0)) break;
       int pg = -1;  // slot past the context: reload a valid page, its keys are masked
+      bool gran = true;
       if (lane < ppc) {
         const int tok = c * kChunk + lane * p.ps;
         if (tok < p.ctx_len) {
-          pg = table[tok];
+          const int64_t r0 = resolve_page(__ldg(table + tok), p.num_pages);
           const int n = min(p.ps, p.ctx_len - tok);
-          bool bad = pg < 0 || pg >= p.num_pages;
+          gran = r0 >= 0;
           if (p.table_vec && n == p.ps) {
             const int4* v = reinterpret_cast<const int4*>(table + tok);
             for (int s = 0; s < p.ps / 4; ++s) {
               const int4 e = __ldg(v + s);
-              bad |= (e.x != pg) | (e.y != pg) | (e.z != pg) | (e.w != pg);
+              gran &= (resolve_page(e.x, p.num_pages) == r0) & (resolve_page(e.y, p.num_pages) == r0) &
+                      (resolve_page(e.z, p.num_pages) == r0) & (resolve_page(e.w, p.num_pages) == r0);
             }
           } else {
-            for (int s = 1; s < n; ++s) bad |= (table[tok + s] != pg);
+            for (int s = 1; s < n; ++s) gran &= resolve_page(__ldg(table + tok + s), p.num_pages) == r0;
           }
-          if (bad) {
-            record_error(MTP_ERR_DEVICE);
-            if (pg < 0 || pg >= p.num_pages) pg = 0;
-          }
+          pg = (int)r0;
         }
       }
-      const int first = __shfl_sync(0xffffffffu, pg, 0);  // slot 0 of a context chunk is always valid
-      if (lane < ppc) sIds[slot * kMaxPagesPerChunk + lane] = pg < 0 ? first : pg;
+      const bool chunk_gran = __all_sync(0xffffffffu, gran);
+      const int first = __shfl_sync(0xffffffffu, pg, 0);  // slot 0 of a context chunk is always in the context
+      if (lane < ppc) sIds[slot * kMaxPagesPerChunk + lane] = !chunk_gran ? -1 : (pg < 0 ? first : pg);
       __syncwarp();
       if (lane == 0) mbar_arrive(&ids_full[slot]);
     }

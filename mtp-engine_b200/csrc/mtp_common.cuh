@@ -22,6 +22,17 @@ static __device__ int g_dev_error;
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_dev_error, 0, code); }
 
+// A page-table entry resolved the way the reference's eager gathers and
+// write_inplace index the pool with it (torch integer / advanced indexing,
+// mtp_kernels.py:839-848, mtp_engine.py:582-586): ids in [-P, P) are valid
+// and a negative id counts from the end, so the -1 that PagedKVCache leaves
+// in unreserved columns selects page P-1.  Returns -1 for ids outside
+// [-P, P), where the reference raises an IndexError.
+__host__ __device__ __forceinline__ int64_t resolve_page(int32_t id, int64_t num_pages) {
+  const int64_t pg = id < 0 ? (int64_t)id + num_pages : (int64_t)id;
+  return (pg >= 0 && pg < num_pages) ? pg : -1;
+}
+
 // --------------------------------------------------------------------------
 // dtype helpers
 // --------------------------------------------------------------------------

@@ -459,6 +459,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           verify_finalize(ep, threadIdx.x - 64, 128);
           if (threadIdx.x == 64) *ep.counter = 0u;
         }
+      } else if (*last_flag) {
+        // this CTA gave up on a wait: put this rank's keys and ticket back at
+        // rest (the exchange buffers of a peer call are rebuilt on every rank)
+        __threadfence();
+        if (ep.finalize != FIN_CHAIN_PEERS) verify_keys_rest(ep, threadIdx.x - 64, 128);
+        if (threadIdx.x == 64) *ep.counter = 0u;
       }
     }
   }

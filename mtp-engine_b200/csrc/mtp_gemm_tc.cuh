@@ -336,9 +336,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         *last_flag = (ticket == gridDim.x - 1) ? 1 : 0;
       }
       epi_bar_sync();
-      if (*last_flag && !*abort_flag) {
+      if (*last_flag) {
+        // every other CTA has taken its ticket: decode, or after a timeout
+        // only put the keys back at rest; either way the ticket resets, so
+        // the workspace is at rest when the launch ends
         __threadfence();
-        verify_finalize(ep, threadIdx.x - 64, 128);
+        if (!*abort_flag) verify_finalize(ep, threadIdx.x - 64, 128);
+        else verify_keys_rest(ep, threadIdx.x - 64, 128);
         if (threadIdx.x == 64) *ep.counter = 0u;
       }
     }

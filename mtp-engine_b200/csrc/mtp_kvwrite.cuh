@@ -8,9 +8,10 @@
 // with node(b, t) = node_idx[b, t] (e.g. the accepted path of a draft tree)
 // or t.  One warp per row; 16-byte chunks when source and pool share a dtype
 // and both are aligned, else element by element with conversion (the
-// reference casts with .to(self.dtype), line 584).  A page id outside the
-// pool or a node index outside the source skips the row and records
-// MTP_ERR_DEVICE.
+// reference casts with .to(self.dtype), line 584).  Page ids resolve like the
+// reference's integer indexing (resolve_page: -1 selects the last page); an
+// id outside [-P, P) or a node index outside the source skips the row and
+// records MTP_ERR_DEVICE.
 #pragma once
 
 #include "mtp_common.cuh"
@@ -42,9 +43,9 @@ __global__ void __launch_bounds__(256) paged_kv_write_kernel(KvWriteArgs a) {
   const int64_t b = row / (a.n * a.H);
   if (a.count && t >= (int64_t)a.count[b]) return;
   const int64_t logical = a.start + t;
-  const int32_t page = a.page_table[b * a.table_stride + logical];
+  const int64_t page = resolve_page(a.page_table[b * a.table_stride + logical], a.num_pages);
   const int64_t node = a.node_idx ? (int64_t)a.node_idx[b * a.n + t] : t;
-  if (page < 0 || page >= a.num_pages || node < 0 || node >= a.src_len) {
+  if (page < 0 || node < 0 || node >= a.src_len) {
     if (lane == 0) record_error(MTP_ERR_DEVICE);
     return;
   }

@@ -76,8 +76,8 @@ __global__ void __launch_bounds__(kThreads) sq_attention_kernel(Args a) {
     int64_t off = 0;
     if (keep) {
       if (a.paged) {
-        const int32_t page = a.page_table[b * a.table_stride + j];
-        if (page < 0 || page >= a.num_pages) {
+        const int64_t page = resolve_page(a.page_table[b * a.table_stride + j], a.num_pages);
+        if (page < 0) {
           record_error(MTP_ERR_DEVICE);
           keep = false;
         } else {

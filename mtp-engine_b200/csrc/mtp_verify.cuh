@@ -85,6 +85,14 @@ __device__ inline void verify_finalize(const GemmEpilogue& ep, int tid, int nthr
   }
 }
 
+// The keys of a verify whose CTAs gave up on a bounded wait, put back at
+// rest without decoding: that call's outputs are undefined (the error word
+// holds MTP_ERR_TIMEOUT), the next call on the workspace runs normally.
+__device__ inline void verify_keys_rest(const GemmEpilogue& ep, int tid, int nthreads) {
+  const int64_t n = ep.finalize == FIN_CHAIN ? ep.B * ep.S : ep.B;
+  for (int64_t i = tid; i < n; i += nthreads) ep.keys[i] = KEY_EMPTY;
+}
+
 __global__ void verify_finalize_kernel(GemmEpilogue ep) {
   verify_finalize(ep, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
@@ -195,9 +203,12 @@ __global__ void __launch_bounds__(256)
   for (int w = 1; w < (int)(blockDim.x >> 5); ++w) n = min(n, red[w]);
   n = max(0, min(n, (int)D));
   const int64_t width = n == D ? D : (int64_t)n + 1;
-  for (int64_t i = threadIdx.x; i < B * width; i += blockDim.x) {
-    const int64_t b = i / width, j = i - b * width;
-    step_tokens[b * ld + j] = j < n ? draft[b * D + j] : corrected[b];
+  // every column of [0, min(ld, D + 1)) is written: tokens up to width, then
+  // -1 (no token), so a replayed step leaves the same bytes as an eager one
+  const int64_t cols = ld < D + 1 ? ld : D + 1;
+  for (int64_t i = threadIdx.x; i < B * cols; i += blockDim.x) {
+    const int64_t b = i / cols, j = i - b * cols;
+    step_tokens[b * ld + j] = j >= width ? -1 : (j < n ? draft[b * D + j] : corrected[b]);
   }
   if (threadIdx.x == 0) {
     info[0] = n;

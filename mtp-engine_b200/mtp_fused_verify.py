@@ -101,7 +101,8 @@ def verify_step(draft: torch.Tensor, accepted_n: torch.Tensor,
     n = accepted_n.min() (one rollback index for the batch); the step's new
     tokens are draft[:, :n] followed by corrected when n < D, else draft.
     Returns (step_tokens [B, D+1] int32, info [2] int32 = (n, width)); the new
-    tokens are step_tokens[:, :width].  Nothing is read back to the host, so
+    tokens are step_tokens[:, :width] and the columns after them hold -1 (no
+    token).  Nothing is read back to the host, so
     a loop can stay on the device (or read the 8 bytes of info once)."""
     dev = _N.require_cuda(draft, accepted_n, corrected)
     draft = draft.contiguous().to(torch.int32)

@@ -170,12 +170,39 @@ class _PeerExchange:
 _EXCHANGES = {}
 
 
+def _invalidate_exchanges(device: torch.device) -> None:
+    """A bounded wait ran out on `device` (seen by _mtp_native.device_status):
+    its peer exchanges may be one call out of step with the other ranks'."""
+    for key, ex in _EXCHANGES.items():
+        if key[1] == device.index:
+            ex.stale = True
+
+
+_N.on_timeout(_invalidate_exchanges)
+
+
+def reset_exchanges() -> None:
+    """Forget this rank's peer-exchange buffers; the next p2p / fused
+    vocab-parallel verify builds new ones at rest (a collective step).  After
+    a timeout every rank must call it, between the same two verify calls:
+    a rank that gave up on a wait is one call out of step with its peers."""
+    _EXCHANGES.clear()
+
+
+def _check_fresh(ex) -> None:
+    if getattr(ex, "stale", False):
+        raise _N.MTPError("a bounded wait ran out in an earlier peer-exchange verify on this device; call "
+                          "mtp_parallel.reset_exchanges() on every rank before the next vocab-parallel verify")
+
+
 def _peer_exchange(dev: torch.device, rows: int, prim: "ParallelPrimitives") -> _PeerExchange:
     # the buffer layout depends on rows (flags follow the keys), so a buffer is
     # used for exactly one row count; every rank makes the same calls, so all
     # ranks rebuild together
     key = ("p2p", dev.index, id(prim.group), prim.tp_size)
     ex = _EXCHANGES.get(key)
+    if ex is not None:
+        _check_fresh(ex)
     if ex is None or ex.rows != rows:
         ex = _PeerExchange(dev, rows, prim)
         _EXCHANGES[key] = ex
@@ -208,6 +235,8 @@ class _FusedExchange:
 def _fused_exchange(dev: torch.device, rows: int, prim: "ParallelPrimitives") -> _FusedExchange:
     key = ("fused", dev.index, id(prim.group), prim.tp_size)
     ex = _EXCHANGES.get(key)
+    if ex is not None:
+        _check_fresh(ex)
     if ex is None or ex.rows != rows:
         ex = _FusedExchange(dev, rows, prim)
         _EXCHANGES[key] = ex
@@ -531,5 +560,5 @@ def __getattr__(name: str):
 __all__ = [
     "ParallelPrimitives", "get_parallel_primitives", "vocab_shard_range", "shard_lm_head",
     "vocab_parallel_multi_verify", "VocabParallelVerify", "RowParallelLinear", "ColumnParallelLinear",
-    "key_index", "NcclCommunicator", "vocab_parallel_multi_verify_nccl",
+    "key_index", "NcclCommunicator", "vocab_parallel_multi_verify_nccl", "reset_exchanges",
 ]

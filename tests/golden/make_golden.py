@@ -82,6 +82,10 @@ def main():
         import mtp_engine
         make_paged_kv_write(torch, mtp_engine)
         return
+    if args.only == "tree_paged_reserve":
+        import mtp_engine
+        make_tree_paged_reserve(torch, mk, mtp_engine)
+        return
 
     # ---------------------------------------------------------------- rmsnorm_linear fp32
     torch.manual_seed(1)  # test_engine.py:5
@@ -279,6 +283,7 @@ def main():
     make_tree_attn_rmsnorm_linear(torch, mk)
     import mtp_engine
     make_paged_kv_write(torch, mtp_engine)
+    make_tree_paged_reserve(torch, mk, mtp_engine)
     make_quant_attention_int4(torch, mk)
 
 
@@ -369,6 +374,65 @@ def make_paged_kv_write(torch, mtp_engine):
                     f"{name}_page_table": kv.page_table.numpy(), f"{name}_k_new": f32(k_new),
                     f"{name}_v_new": f32(v_new), f"{name}_start": np.array([start], np.int64)})
     save("paged_kv_write.npz", **out)
+
+
+# token counts passed to PagedKVCache.reserve, then the logical columns swapped
+RESERVES = (5, 1, 1, 16, 7, 40, 3, 50, 30, 9)
+SWAPS = ((3, 100), (20, 21), (0, 140), (64, 65), (17, 161))
+
+
+def make_tree_paged_reserve(torch, mk, mtp_engine):
+    """Paged tree attention over a page table that the reference's own
+    PagedKVCache built (mtp_engine.py:523-610): reserve() with token counts
+    that are not multiples of page_size, then swap_logical_pages().  The
+    table is then not page-granular (one page slot's 16 tokens come from
+    several pages), and the columns that reserve() never reaches keep -1,
+    which torch indexing reads as page P-1.  Output: the composite of the
+    reference's eager functions -- the gather of _eager_paged_attention
+    (mtp_kernels.py:839-848), then _eager_tree_attention per tree node
+    (859-872), GQA by repeat_interleave -- with head_dim 128 and page_size
+    16, the shapes the tensor-core kernel takes; plus _eager_paged_attention
+    itself (the single-query operator) on the same table.  K/V/Q values are
+    bf16-representable (stored as bf16 bits)."""
+    torch.manual_seed(23)
+    B, Hq, Hkv, D, ps, P = 2, 8, 2, 128, 16, 24
+    G = Hq // Hkv
+    bf = lambda t: t.to(torch.bfloat16).to(torch.float32)
+    kv = mtp_engine.PagedKVCache(batch=B, num_heads=Hkv, head_dim=D, num_pages=P, page_size=ps,
+                                 device=torch.device("cpu"), dtype=torch.float32)
+    kv.k_pages.copy_(bf(torch.randn(kv.k_pages.shape)))
+    kv.v_pages.copy_(bf(torch.randn(kv.v_pages.shape)))
+    for n in RESERVES:
+        kv.reserve(n)
+    ctx = kv._next_logical
+    for a, b_ in SWAPS:
+        kv.swap_logical_pages(a, b_)
+    tree = mtp_engine.SpeculativeDraftTree(depth=4, max_branches=2, mode="tree")
+    T = tree.max_nodes
+    qt = bf(torch.randn(B, T, Hq, D))
+    tk = bf(torch.randn(B, Hkv, T, D))
+    tv = bf(torch.randn(B, Hkv, T, D))
+    scale = 1.0 / math.sqrt(D)
+    page = kv.page_table[:, :ctx].long()
+    slot = torch.arange(ctx) % ps
+    bi = torch.arange(B)[:, None, None].expand(B, Hkv, ctx)
+    hi = torch.arange(Hkv)[None, :, None].expand(B, Hkv, ctx)
+    kc = kv.k_pages[page.unsqueeze(1).expand(B, Hkv, ctx), bi, hi, slot[None, None].expand(B, Hkv, ctx)]
+    vc = kv.v_pages[page.unsqueeze(1).expand(B, Hkv, ctx), bi, hi, slot[None, None].expand(B, Hkv, ctx)]
+    Kall = torch.cat([kc, tk], dim=2).repeat_interleave(G, dim=1)
+    Vall = torch.cat([vc, tv], dim=2).repeat_interleave(G, dim=1)
+    out_t = torch.empty(B, T, Hq, D)
+    for n in range(T):
+        mask_n = torch.cat([torch.ones(ctx), tree.tree_mask[n]])
+        out_t[:, n] = mk._eager_tree_attention(qt[:, n], Kall, Vall, mask_n, scale)
+    q1 = bf(torch.randn(B, Hkv, D))
+    out1 = mk._eager_paged_attention(q1, kv.k_pages, kv.v_pages, kv.page_table[:, :ctx].contiguous(), ps, scale)
+    save("tree_paged_reserve.npz", q_bits=bits16(qt.to(torch.bfloat16)),
+         k_pages_bits=bits16(kv.k_pages.to(torch.bfloat16)), v_pages_bits=bits16(kv.v_pages.to(torch.bfloat16)),
+         page_table=kv.page_table.numpy(), tree_k_bits=bits16(tk.to(torch.bfloat16)),
+         tree_v_bits=bits16(tv.to(torch.bfloat16)), tree_mask=f32(tree.tree_mask),
+         meta=np.array([ctx, ps], dtype=np.int64), out=f32(out_t),
+         q1_bits=bits16(q1.to(torch.bfloat16)), out1=f32(out1))
 
 
 def make_tree_attn_rmsnorm_linear(torch, mk):

@@ -147,24 +147,36 @@ def test_fused_exchange_single_rank_matches_verify(mods):
 
 
 def test_fused_exchange_missing_peer_times_out(mods):
+    """After the fused exchange gives up on a peer, the verify that shares
+    its workspace (ticket) gives exactly its earlier result -- first without
+    anyone reading the device status, then after device_status() has reported
+    the timeout and dropped the cached workspaces."""
     N, mv = mods
     hid, w, draft = inputs(4)
     B, S, _ = hid.shape
     dev = hid.device
+    ref = mv.fused_multi_verify(hid, w, draft)
+    torch.cuda.synchronize()
     N.device_status(dev)
     bufs, peers = fused_buffers(N, B * S, 2, 2)  # rank 1 never runs
     t0 = time.perf_counter()
     shard_fused(N, hid, w, draft, peers, 0, 2)
     torch.cuda.synchronize()
     waited = time.perf_counter() - t0
+    after = mv.fused_multi_verify(hid, w, draft)  # same workspace, status not read yet
+    torch.cuda.synchronize()
+    for a, b in zip(after, ref):
+        assert torch.equal(a, b)
     assert N.device_status(dev) == ERR_TIMEOUT
     assert 1.0 < waited < 30.0
     # this rank's keys of the failed call are back at rest, and the context works
     rows = B * S
     assert bool((bufs[0][:2 * rows] == INT64_MIN).all())
-    ref = mv.fused_multi_verify(hid, w, draft)
+    again = mv.fused_multi_verify(hid, w, draft)  # new workspace after the reset
     torch.cuda.synchronize()
-    assert N.device_status(dev) == 0 and int(ref[1].min()) >= 0
+    for a, b in zip(again, ref):
+        assert torch.equal(a, b)
+    assert N.device_status(dev) == 0
 
 
 def test_fused_exchange_streamk_single_rank(mods):

@@ -163,6 +163,69 @@ def test_attention_golden(mods, golden):
     assert np.abs(np32(o) - g["out"]).max() < 1e-4
 
 
+def test_tree_paged_reserve_built_table(mods, golden):
+    """Page table from the reference's own PagedKVCache after reserve() of
+    5, 1, 1, 16, 7, ... tokens and swap_logical_pages(): every context chunk
+    is gathered token by token by the tensor-core kernel (and -1 entries read
+    page P-1, as torch indexing does); the single-query operator on the same
+    table through both decode kernels."""
+    import _mtp_native as N
+    mk, _, _ = mods
+    g = golden("tree_paged_reserve.npz")
+    ctx, ps = (int(v) for v in g["meta"])
+    bf = lambda a: torch.tensor(a.view(np.int16), device=dev()).view(torch.bfloat16)
+    N.device_status(dev())
+    o = mk.fused_tree_attention_paged(bf(g["q_bits"]), bf(g["k_pages_bits"]), bf(g["v_pages_bits"]),
+                                      torch.tensor(g["page_table"], device=dev()), bf(g["tree_k_bits"]),
+                                      bf(g["tree_v_bits"]), torch.tensor(g["tree_mask"], device=dev()), ctx_len=ctx)
+    check_rel(np32(o), g["out"])
+    assert N.device_status(dev()) == 0
+    table = torch.tensor(g["page_table"][:, :ctx], device=dev())
+    prev = N.decode_kernel()
+    for ver in (1, 2):
+        N.set_decode_kernel(ver)
+        try:
+            o1 = mk.fused_paged_attention(bf(g["q1_bits"]), bf(g["k_pages_bits"]), bf(g["v_pages_bits"]), table, ps)
+        finally:
+            N.set_decode_kernel(prev)
+        check_rel(np32(o1), g["out1"])
+        assert N.device_status(dev()) == 0
+
+
+@pytest.mark.parametrize("mode", ["per_token", "mixed"])
+def test_tree_paged_per_token_tables(mods, mode):
+    """Tables that are not page-granular at a config-4-like shape (GQA 4,
+    64 tree nodes, 16-token pages): every token's page drawn on its own in
+    [-P, P) ("per_token"), or page-granular chunks with one token moved in
+    every other 128-token chunk ("mixed"), so both gathers of the
+    tensor-core kernel run in one launch."""
+    import _mtp_native as N
+    mk, _, _ = mods
+    B, Hq, Hkv, D, ps, ctx, P = 2, 32, 8, 128, 16, 1000, 128
+    g = torch.Generator(device=dev()).manual_seed(31)
+    rnd = lambda *shape: torch.randn(*shape, generator=g, device=dev()).to(torch.bfloat16)
+    kp, vp = rnd(P, B, Hkv, ps, D), rnd(P, B, Hkv, ps, D)
+    rng = np.random.default_rng(31)
+    if mode == "per_token":
+        table = rng.integers(-P, P, size=(B, ctx))
+    else:
+        pages = rng.permutation(P)[: (ctx + ps - 1) // ps * B].reshape(B, -1)
+        table = np.repeat(pages, ps, axis=1)[:, :ctx]
+        for c in range(0, ctx, 256):
+            table[:, c + 5] = rng.integers(-P, P, size=B)
+    table = np.ascontiguousarray(table, dtype=np.int32)
+    _, tm = O.draft_tree(16, 4, "tree")
+    T = tm.shape[0]
+    q, tk, tv = rnd(B, T, Hq, D), rnd(B, Hkv, T, D), rnd(B, Hkv, T, D)
+    N.device_status(dev())
+    o = mk.fused_tree_attention_paged(q, kp, vp, torch.tensor(table, device=dev()), tk, tv,
+                                      torch.tensor(tm, device=dev()), ctx_len=ctx)
+    ref = O.tree_attention_paged_fast(np32(q), np32(kp), np32(vp), table, ctx, ps, np32(tk), np32(tv), tm,
+                                      1.0 / math.sqrt(D))
+    check_rel(np32(o), ref)
+    assert N.device_status(dev()) == 0
+
+
 # --------------------------------------------------------------------------- #
 # bf16 / fp8 tensor-core paths
 # --------------------------------------------------------------------------- #

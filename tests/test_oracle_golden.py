@@ -181,6 +181,23 @@ def test_tree_paged_attention(golden):
     np.testing.assert_allclose(of, g["out"], rtol=1e-5, atol=1e-5)
 
 
+def test_tree_paged_attention_reserve_built_table(golden):
+    """A page table from the reference's own PagedKVCache after unaligned
+    reserve() calls and swap_logical_pages(): not page-granular, with -1
+    entries inside the context that index page P-1 as torch does."""
+    g = golden("tree_paged_reserve.npz")
+    ctx, ps = (int(v) for v in g["meta"])
+    bf = O.bf16_bits_to_f32
+    args = (bf(g["q_bits"]), bf(g["k_pages_bits"]), bf(g["v_pages_bits"]), g["page_table"], ctx, ps,
+            bf(g["tree_k_bits"]), bf(g["tree_v_bits"]), g["tree_mask"], 1.0 / math.sqrt(128))
+    assert (g["page_table"][:, :ctx] < 0).any()  # the wrap is exercised
+    np.testing.assert_allclose(O.tree_attention_paged(*args), g["out"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(O.tree_attention_paged_fast(*args), g["out"], rtol=1e-5, atol=1e-5)
+    o1 = O.paged_attention(bf(g["q1_bits"]), bf(g["k_pages_bits"]), bf(g["v_pages_bits"]),
+                           g["page_table"][:, :ctx], ps, 1.0 / math.sqrt(128))
+    np.testing.assert_allclose(o1, g["out1"], rtol=1e-5, atol=1e-5)
+
+
 @pytest.mark.parametrize("key,args", [("tree_16_4", (16, 4, "tree")), ("tree_4_8", (4, 8, "tree")),
                                       ("trunk_4_8", (4, 8, "trunk")), ("tree_4_2", (4, 2, "tree"))])
 def test_draft_tree(golden, key, args):

@@ -49,3 +49,4 @@ def test_device_step_matches_oracle():
         n_dev, width = (int(x) for x in info.cpu())
         assert n_dev == n and width == ref.shape[1]
         assert np.array_equal(st[:, :width].cpu().numpy(), ref)
+        assert (st[:, width:] == -1).all()  # the columns after the step's tokens hold "no token"

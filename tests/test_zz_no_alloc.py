@@ -86,6 +86,21 @@ def test_noalloc_matches_regular_twice(N, dtype):
     assert N.device_status(dev) == 0
 
 
+def test_noalloc_single_position(N):
+    """S == 1 (no drafts: draft and accept may be NULL): only corrected and
+    accepted_n = 0 come out, equal to the regular entry's, twice in a row."""
+    dev = torch.device("cuda", 0)
+    for seed in (13, 14):
+        hid, w, bias, draft = _inputs(seed, 24, 1, 768, 5003, torch.bfloat16, dev)
+        ref = _regular(N, hid, w, bias, draft)
+        got = _noalloc(N, hid, w, bias, draft)
+        torch.cuda.synchronize()
+        for x, y in zip(got, ref):
+            assert torch.equal(x, y)
+        assert int(got[1].abs().max()) == 0
+    assert N.device_status(dev) == 0
+
+
 def test_noalloc_rejects_oversized(N):
     dev = torch.device("cuda", 0)
     before = N.lib().mtp_launch_count()
@@ -94,4 +109,8 @@ def test_noalloc_rejects_oversized(N):
                                                 N.stream_handle(dev))
     assert st == 1  # MTP_ERR_SHAPE
     assert b"exceeds" in N.lib().mtp_last_error()
+    # B * S past INT64_MAX must not wrap into the accepted range
+    st = N.lib().mtp_fused_multi_verify_noalloc(None, 1, None, 1, None, 0, None, None, None, None, 2 ** 62 + 1, 4,
+                                                64, 128, N.stream_handle(dev))
+    assert st == 1
     assert N.lib().mtp_launch_count() == before
