@@ -7,12 +7,13 @@ A step is one pass of the hot path over the benchmark workloads:
      64-node tree (config 4)
   3. fused_multi_verify, bf16, B=64 S=6 K=4096 V=128256 (config 5)
 and verifies B*S = 384 candidate tokens.  On N GPUs (torchrun, one rank per
-GPU) the same total work is split tensor-parallel: stage 1 by output
-columns, stage 2 by KV heads, stage 3 by vocabulary with one all-reduce(MAX)
-of packed (logit, index) keys over NCCL -- strong scaling.  With
---scaling weak, every rank runs stages 1 and 2 whole on its own batch and
-stage 3 verifies every rank's sequences against its vocabulary block
-(candidates all-gathered, keys all-reduced) -- weak scaling.
+GPU) every rank runs stages 1 and 2 whole on its own batch and stage 3
+verifies every rank's sequences against its vocabulary block of the
+lm_head (candidates all-gathered, packed (logit, index) keys all-reduced
+with MAX over NCCL) -- weak scaling, the north star's layout, where only
+the lm_head is sharded.  With --scaling strong the 1-GPU job is split
+tensor-parallel instead: stage 1 by output columns, stage 2 by KV heads,
+stage 3 by vocabulary.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--scaling strong|weak] [--exchange nccl|p2p|fused|abi]
@@ -652,11 +653,14 @@ def run_ours(args):
                          "for each step's result",
                 "one_graph_per_step": bool(args.e2e_graph and world == 1)},
         "gpu_launches": launches,
+        "parity": parity,
         "clocks": clocks,
         "kernels": kernels,
         "device_status": status,
     }
     print(json.dumps(line), flush=True)
+    if not parity["ok"]:
+        print(f"bench: verify outputs differ from the fp32 checker: {parity}", file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -1153,6 +1157,27 @@ def run_profile_case(args):
             w = (0.02 * torch.randn(V, K, generator=g, device=dev)).to(torch.bfloat16)
             d = torch.randint(0, V, (B, S - 1), device=dev, dtype=torch.int32)
             fn = lambda: mv.fused_multi_verify(hid, w, d)
+        elif case in ("verify_rank8_weak", "verify_rank8_strong"):
+            # one rank's shard GEMM of an 8-way vocab-parallel verify: every
+            # rank's candidates (weak: 8 x 384 rows) against V/8 lm_head rows
+            import _mtp_native as Nn
+            S, K, V = C5["S"], C5["K"], C5["V"]
+            rows = C5["B"] * S * (8 if case.endswith("weak") else 1)
+            Vr = V // 8
+            hid = torch.randn(rows, K, generator=g, device=dev).to(torch.bfloat16)
+            w = (0.02 * torch.randn(Vr, K, generator=g, device=dev)).to(torch.bfloat16)
+            keys = torch.full((rows,), -(2 ** 63), dtype=torch.int64, device=dev)
+            fn = lambda: Nn.check(Nn.lib().mtp_verify_shard_keys(Nn.ptr(hid), Nn.DT_BF16, Nn.ptr(w), Nn.DT_BF16,
+                                                                 None, 0, Nn.ptr(keys), rows, K, Vr, 0,
+                                                                 Nn.stream_handle(dev)), "shard keys")
+        elif case == "fp8":
+            M, K, Nn_ = 1024, 8192, 28672
+            x = torch.randn(M, K, generator=g, device=dev)
+            x = x * (448.0 / x.abs().amax(dim=1, keepdim=True))
+            xq, sx = mk.quantize_fp8_rows(x)
+            wq, sw = mk.quantize_fp8_rows(0.02 * torch.randn(Nn_, K, generator=g, device=dev))
+            del x
+            fn = lambda: mk.fused_rmsnorm_linear_fp8(xq, wq, sw, x_scale=sx, out_dtype=torch.bfloat16)
         else:  # rms
             M, K, Nn = C2["M"], C2["K"], C2["N"]
             x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
@@ -1185,10 +1210,12 @@ def main():
                          "library's own NCCL communicator")
     ap.add_argument("--e2e-graph", action="store_true",
                     help="1 GPU: capture the end-to-end step (uploads, stages, read-back) as one CUDA graph")
-    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
-                    help="N > 1: strong = the 1-GPU job split tensor-parallel; weak = configs 2 and 4 whole on "
-                         "every GPU, the verify over every rank's sequences with the lm_head vocab-sharded")
-    ap.add_argument("--profile-case", choices=["verify", "rms", "attention"], default=None,
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="weak",
+                    help="N > 1: weak (default, the north star's layout) = configs 2 and 4 whole on every GPU, "
+                         "the verify over every rank's sequences with the lm_head vocab-sharded; strong = the "
+                         "1-GPU job split tensor-parallel")
+    ap.add_argument("--profile-case", choices=["verify", "rms", "attention", "fp8", "verify_rank8_weak",
+                                               "verify_rank8_strong"], default=None,
                     help="call one operator at its benchmark config --steps times (the workload of the ncu "
                          "captures in profiles/)")
     ap.add_argument("--sweep-only", default="",

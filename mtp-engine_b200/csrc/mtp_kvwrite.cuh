@@ -11,7 +11,8 @@
 // reference casts with .to(self.dtype), line 584).  Page ids resolve like the
 // reference's integer indexing (resolve_page: -1 selects the last page); an
 // id outside [-P, P) or a node index outside the source skips the row and
-// records MTP_ERR_DEVICE.
+// records MTP_ERR_DEVICE.  When several tokens of one call map to the same
+// (page, slot), the last of them is written, as in the reference's loop.
 #pragma once
 
 #include "mtp_common.cuh"
@@ -49,6 +50,17 @@ __global__ void __launch_bounds__(256) paged_kv_write_kernel(KvWriteArgs a) {
     if (lane == 0) record_error(MTP_ERR_DEVICE);
     return;
   }
+  // The reference writes token after token, so when two tokens of this call
+  // land on one (page, slot) -- a -1 column aliasing page P-1, or a table
+  // that maps two pages' slots to one page -- the later token stays.  Tokens
+  // t < t2 share a slot only if t2 - t is a multiple of page_size: the lanes
+  // check t + page_size, t + 2 page_size, ... and this row yields if any of
+  // them (within its sequence's count) resolves to the same page.
+  const int64_t nb = a.count ? min(a.n, (int64_t)a.count[b]) : a.n;
+  bool later = false;
+  for (int64_t t2 = t + (int64_t)(lane + 1) * a.page_size; t2 < nb; t2 += 32 * a.page_size)
+    later |= resolve_page(a.page_table[b * a.table_stride + a.start + t2], a.num_pages) == page;
+  if (__any_sync(0xffffffffu, later)) return;
   const int64_t dst = ((((int64_t)page * a.B + b) * a.H + h) * a.page_size + logical % a.page_size) * a.D;
   const int64_t src = ((b * a.H + h) * a.src_len + node) * a.D;
   if (a.vec) {
