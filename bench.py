@@ -837,6 +837,8 @@ def run_sweep(args):
         return statistics.median(ts)
 
     def cpu_time(fn, budget=8.0):
+        if args.no_cpu_baseline:
+            return float("nan")
         fn()
         ts, t0 = [], time.perf_counter()
         while not ts or (time.perf_counter() - t0 < budget and len(ts) < 5):

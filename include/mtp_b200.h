@@ -130,11 +130,11 @@ int mtp_set_attn_kernel(int version);
 int mtp_attn_kernel(void);
 
 /* Process-wide choice of the single-query kernel behind mtp_tree_attention
- * and mtp_paged_attention: 1 (default) = one warp per key with scalar loads;
- * 2 = 16-byte loads with several keys in flight per lane and P V split over
- * key groups, for 16-bit K/V with a power-of-two head size up to 256 (other
- * shapes run kernel 1).  MTP_DECODE_KERNEL=2 sets the initial value.
- * Returns MTP_ERR_ARG for other values. */
+ * and mtp_paged_attention: 2 (default) = 16-byte loads with several keys in
+ * flight per lane and P V split over key groups, for 16-bit K/V with a
+ * power-of-two head size up to 256 (other shapes run kernel 1); 1 = one
+ * warp per key with scalar loads, every shape.  MTP_DECODE_KERNEL=1 sets the
+ * initial value.  Returns MTP_ERR_ARG for other values. */
 int mtp_set_decode_kernel(int version);
 int mtp_decode_kernel(void);
 
