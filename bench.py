@@ -17,7 +17,7 @@ stage 3 by vocabulary.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--scaling strong|weak] [--exchange nccl|p2p|fused|abi]
-                    [--gemm-schedule dp|streamk] [--gemm-tile-rows 128|256]
+                    [--gemm-schedule dp|streamk]
     python bench.py --sweep [--sweep-only SECTIONS] [--compare]   # one line per config
     python bench.py --profile-case verify|rms|attention --steps K # the ncu capture workloads
 
@@ -252,7 +252,6 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)  # before any workspace exists
-    N.set_gemm_tile_rows(1 if args.gemm_tile_rows == 256 else 0)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
@@ -645,7 +644,7 @@ def run_ours(args):
         "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) activations / KV, random-init weights of the benchmark shapes",
         "config": dict(arm_config(world, weak, args), gemm_schedule=args.gemm_schedule,
-                       gemm_tile_rows=args.gemm_tile_rows, exchange=args.exchange if world > 1 else "none"),
+                       exchange=args.exchange if world > 1 else "none"),
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -817,7 +816,6 @@ def run_sweep(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
-    N.set_gemm_tile_rows(1 if args.gemm_tile_rows == 256 else 0)
     peaks = load_peaks()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     f32 = lambda t: t.detach().float().cpu().numpy()
@@ -849,7 +847,7 @@ def run_sweep(args):
 
     def emit(name, units, unit, t, bound, achieved, peak, peak_src, cpu_units, cpu_t, extra=None):
         line = {"sweep": True, "config": name, "metric": f"{unit} ({name})", "value": units / t, "unit": unit,
-                "gemm_schedule": args.gemm_schedule, "gemm_tile_rows": args.gemm_tile_rows,
+                "gemm_schedule": args.gemm_schedule,
                 "ms": t * 1e3, "dtype": extra.pop("dtype") if extra and "dtype" in extra else "bf16",
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak,
                              "unit": "TFLOP/s" if bound == "tensor" else "GB/s", "frac": achieved / peak,
@@ -863,21 +861,16 @@ def run_sweep(args):
     iters = max(5, min(args.steps, 50))
     # --compare: each GEMM config under both schedules, config 4 under both
     # attention kernels (one line per variant)
-    # GEMM variants: (label, schedule, tile-rows mode); "dp-256rows" = data-parallel 256 x 256 tiles
-    base_rows = 1 if args.gemm_tile_rows == 256 else 0
-    gemm_variants = ((("dp", 0, 0), ("streamk", 1, 0), ("dp-256rows", 0, 1)) if args.compare else
-                     ((args.gemm_schedule + ("-256rows" if base_rows else ""),
-                       1 if args.gemm_schedule == "streamk" else 0, base_rows),))
-    attn_variants = (1, 2) if args.compare else (N.attn_kernel(),)
+    # GEMM variants: (label, schedule)
+    gemm_variants = ((("dp", 0), ("streamk", 1)) if args.compare else
+                     ((args.gemm_schedule, 1 if args.gemm_schedule == "streamk" else 0),))
 
     def timed_gemm(fn):
         out = []
-        for label, sched, rows_mode in gemm_variants:
+        for label, sched in gemm_variants:
             N.set_gemm_schedule(sched)
-            N.set_gemm_tile_rows(rows_mode)
             out.append((label, time_call(fn, iters)))
         N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
-        N.set_gemm_tile_rows(base_rows)
         return out
 
     def sec_config1():
@@ -968,18 +961,14 @@ def run_sweep(args):
         tk = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
         tv = torch.randn(B, Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
         tmd = torch.tensor(tm, device=dev)
-        atimes = []
-        for v in attn_variants:
-            N.set_attn_kernel(v)
-            atimes.append((v, time_call(lambda: mk.fused_tree_attention_paged(q, kp, vp, tdev, tk, tv, tmd), iters)))
+        t4 = time_call(lambda: mk.fused_tree_attention_paged(q, kp, vp, tdev, tk, tv, tmd), iters)
         pages0 = table[0].view(-1, ps)[:, 0].long()
         kps, vps = f32(kp[pages0.to(dev)][:, 0:1]), f32(vp[pages0.to(dev)][:, 0:1])
         tab0 = np.repeat(np.arange(pages0.numel(), dtype=np.int32), ps)[None, :]
         q0, tk0, tv0 = f32(q[0:1]), f32(tk[0:1]), f32(tv[0:1])
         ct = cpu_time(lambda: O.tree_attention_paged_fast(q0, kps, vps, tab0, ctx, ps, tk0, tv0, tm, 1 / math.sqrt(D)))
-        for v, t in atimes:
-            emit("config4_tree_attention", B * T, "tree-node queries/s", t, "hbm", C4_BYTES / t / 1e9, peaks["hbm"],
-                 "measured hbm_gbs", T, ct, {"tflops": C4_FLOP / t / 1e12, "attn_kernel": v})
+        emit("config4_tree_attention", B * T, "tree-node queries/s", t4, "hbm", C4_BYTES / t4 / 1e9, peaks["hbm"],
+             "measured hbm_gbs", T, ct, {"tflops": C4_FLOP / t4 / 1e12})
         del kp, vp
 
     def sec_config5():
@@ -1133,7 +1122,6 @@ def run_profile_case(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)
-    N.set_gemm_tile_rows(1 if args.gemm_tile_rows == 256 else 0)
     case = args.profile_case
     if case == "attention":
         B, Hq, Hkv, D, ps, ctx, P = C4["B"], C4["Hq"], C4["Hkv"], C4["D"], C4["ps"], C4["ctx"], C4["P"]
@@ -1225,13 +1213,10 @@ def main():
                          "ref_bench_fusion_verify, operators; prefixes match), so sections can run in separate "
                          "processes")
     ap.add_argument("--compare", action="store_true",
-                    help="with --sweep: every GEMM config under both schedules, config 4 under both attention "
-                         "kernels, the single-query lines under both decode kernels")
+                    help="with --sweep: every GEMM config under both schedules, the single-query lines under "
+                         "both decode kernels")
     ap.add_argument("--gemm-schedule", choices=["dp", "streamk"], default="dp",
                     help="tensor-core GEMM schedule: whole tiles per CTA, or stream-K where it is faster")
-    ap.add_argument("--gemm-tile-rows", type=int, choices=[128, 256], default=128,
-                    help="rows per data-parallel GEMM tile: 256 = 256 x 256 tiles (two MMAs share each weight "
-                         "stage) where the cost model expects them to be faster")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

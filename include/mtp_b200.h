@@ -97,37 +97,16 @@ int mtp_device_status(void* stream, int* code_out, int clear);
 int mtp_set_gemm_schedule(int mode);
 int mtp_gemm_schedule(void);
 
-/* Process-wide row height of the tensor-core GEMM's data-parallel tiles
- * (mtp_rmsnorm_linear, its FP8 variant, the verify GEMMs): 0 (default) =
- * 128-row tiles; 1 = 256 x 256 tiles, two M=128 MMAs per K step sharing the
- * weight stage (a third less operand traffic per FLOP), where a cost model
- * (rounds x max(MMA, operand traffic) per K block) expects them to be faster;
- * 2 = 256-row tiles for every such GEMM with more than 128 rows (for tests).  Results are bit-identical across
- * modes.  The environment variable MTP_GEMM_ROWS (0/1/2) sets the initial
- * value when the Python package loads the library.  Returns MTP_ERR_ARG for
- * other values. */
-int mtp_set_gemm_tile_rows(int mode);
-int mtp_gemm_tile_rows(void);
+/* Test support, host only: the tile width *bn of the tensor-core GEMM of
+ * C[M,N] on `sms` SMs (tiles are 128 rows x *bn columns). */
+int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* bn);
 
-/* Test support, host only: the tile (*rows x *bn) that the data-parallel
- * tensor-core GEMM of C[M,N] would use on `sms` SMs under the current
- * tile-rows mode. */
-int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* rows, int* bn);
-
-/* Test support, host only: walks the data-parallel kernel's tile order
- * (rows = 128 or 256, 256 columns) for every CTA of a `grid`-CTA launch and
- * checks that each tile is taken exactly once.  *max_units (may be NULL)
- * receives the most 128-row halves any one CTA multiplies (its load; a half
- * tile counts 1).  MTP_OK or MTP_ERR_SHAPE (message in mtp_last_error). */
-int mtp_gemm_tile_check(int64_t M, int64_t N, int rows, int grid, int64_t* max_units);
-
-/* Process-wide choice of the paged tree-attention kernel behind
- * mtp_tree_attention_paged: 1 (default) = 128-key chunks; 2 = 64-key chunks
- * with double-buffered scores in tensor memory (shapes it cannot take run
- * kernel 1).  The environment variable MTP_ATTN_KERNEL=2 sets the initial
- * value.  Returns MTP_ERR_ARG for other values. */
-int mtp_set_attn_kernel(int version);
-int mtp_attn_kernel(void);
+/* Test support, host only: walks the tensor-core GEMM's tile order (128 x
+ * 256 tiles, M fastest) for every CTA of a `grid`-CTA launch and checks that
+ * each tile is taken exactly once.  *max_tiles (may be NULL) receives the
+ * most tiles any one CTA takes.  MTP_OK or MTP_ERR_SHAPE (message in
+ * mtp_last_error). */
+int mtp_gemm_tile_check(int64_t M, int64_t N, int grid, int64_t* max_tiles);
 
 /* Process-wide choice of the single-query kernel behind mtp_tree_attention
  * and mtp_paged_attention: 2 (default) = 16-byte loads with several keys in

@@ -62,10 +62,8 @@ SIGNATURES = {
     "mtp_verify_shard_keys_ws": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "mtp_verify_chain_from_keys": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_keys_fill": (_i, [_vp, _i64, _vp]),
-    "mtp_set_gemm_tile_rows": (_i, [_i]),
-    "mtp_gemm_tile_rows": (_i, []),
-    "mtp_gemm_tile_plan": (_i, [_i64, _i64, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
-    "mtp_gemm_tile_check": (_i, [_i64, _i64, _i, _i, ctypes.POINTER(_i64)]),
+    "mtp_gemm_tile_plan": (_i, [_i64, _i64, _i, ctypes.POINTER(_i)]),
+    "mtp_gemm_tile_check": (_i, [_i64, _i64, _i, ctypes.POINTER(_i64)]),
     "mtp_nccl_version": (_i, [ctypes.POINTER(_i)]),
     "mtp_nccl_unique_id": (_i, [_vp]),
     "mtp_nccl_comm_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i]),
@@ -84,8 +82,6 @@ SIGNATURES = {
     "mtp_verify_exchange_chain": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mtp_set_gemm_schedule": (_i, [_i]),
     "mtp_gemm_schedule": (_i, []),
-    "mtp_set_attn_kernel": (_i, [_i]),
-    "mtp_attn_kernel": (_i, []),
     "mtp_set_decode_kernel": (_i, [_i]),
     "mtp_decode_kernel": (_i, []),
     "mtp_gemm_streamk_bytes": (_sz, [_i64, _i64, _i64, _i]),
@@ -121,8 +117,6 @@ def lib() -> ctypes.CDLL:
                     fn.argtypes = args
                 if os.environ.get("MTP_GEMM_STREAMK") == "1":  # before any workspace exists
                     L.mtp_set_gemm_schedule(1)
-                if os.environ.get("MTP_GEMM_ROWS") in ("0", "1", "2"):
-                    L.mtp_set_gemm_tile_rows(int(os.environ["MTP_GEMM_ROWS"]))
                 _lib = L
     return _lib
 
@@ -229,18 +223,6 @@ def gemm_schedule() -> int:
     return int(lib().mtp_gemm_schedule())
 
 
-def gemm_tile_rows() -> int:
-    return int(lib().mtp_gemm_tile_rows())
-
-
-def set_gemm_tile_rows(mode: int) -> None:
-    """0 = 128-row GEMM tiles, 1 = 256 x 256 tiles where the cost model
-    expects them to be faster, 2 = 256-row
-    tiles for every tensor-core GEMM with more than 128 rows (tests).  Needs
-    no workspace change: the tiles use the data-parallel schedule."""
-    check(lib().mtp_set_gemm_tile_rows(int(mode)), "mtp_set_gemm_tile_rows")
-
-
 def set_gemm_schedule(mode: int) -> None:
     """0 = data-parallel tiles, 1 = stream-K where it is faster.  Cached
     RMSNorm-linear workspaces are dropped: one used under schedule 0 may have
@@ -249,15 +231,6 @@ def set_gemm_schedule(mode: int) -> None:
     with _ws_lock:
         for key in [k for k in _ws if k[2] in _GEMM_WS]:
             del _ws[key]
-
-
-def attn_kernel() -> int:
-    return int(lib().mtp_attn_kernel())
-
-
-def set_attn_kernel(version: int) -> None:
-    """1 = the 128-key tree-attention kernel, 2 = the 64-key kernel."""
-    check(lib().mtp_set_attn_kernel(int(version)), "mtp_set_attn_kernel")
 
 
 def decode_kernel() -> int:

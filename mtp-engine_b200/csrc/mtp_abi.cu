@@ -18,7 +18,6 @@
 
 #include "mtp_attention.cuh"
 #include "mtp_attention_tc.cuh"
-#include "mtp_attention_tc2.cuh"
 #include "mtp_gemm_simt.cuh"
 #include "mtp_gemm_sk.cuh"
 #include "mtp_gemm_tc.cuh"
@@ -40,7 +39,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[MTP_NOALLOC_MAX
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 
 // A named NVTX range around each compute entry point, so profilers can select
 // an operator by name (ncu --nvtx --nvtx-include); free when no tool is attached.
@@ -139,11 +138,11 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool fp8, int dt16, int6
 }
 
 // ---------------------------------------------------------------- GEMM launchers
-template <int BN, bool FP8, int FMT, int MH = 1>
+template <int BN, bool FP8, int FMT>
 int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int num_kb, const GemmEpilogue& ep,
                    cudaStream_t s) {
-  auto kern = tc::gemm_tc_kernel<BN, FP8, FMT, MH>;
-  constexpr int smem = tc::Cfg<BN, MH>::SMEM_BYTES;
+  auto kern = tc::gemm_tc_kernel<BN, FP8, FMT>;
+  constexpr int smem = tc::Cfg<BN>::SMEM_BYTES;
   int dev;
   if (int st = current_device(&dev)) return st;
   static bool attr_done[kMaxDevices] = {false};
@@ -151,8 +150,7 @@ int launch_tc_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
     MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_done[dev] = true;
   }
-  constexpr int tile_m = tc::Cfg<BN, MH>::TILE_M;
-  const int tiles = ((M + tile_m - 1) / tile_m) * ((N + BN - 1) / BN);
+  const int tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   kern<<<grid, tc::kThreads, smem, s>>>(ta, tb, M, N, num_kb, ep);
   MTP_LAUNCH_CHECK();
@@ -191,39 +189,6 @@ int launch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, in
     case 128: return launch_tc_inst<128, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
     default: return launch_tc_inst<64, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
   }
-}
-
-// Process-wide row height of the data-parallel tiles (mtp_set_gemm_tile_rows):
-// 0 = 128-row tiles (default); 1 = 256-row tiles x 256 columns where
-// use_tall_tiles() expects them to pay; 2 = 256-row tiles for every
-// tensor-core GEMM with more than 128 rows (tests).
-std::atomic<int> g_gemm_rows{0};
-
-// Cycles per K block of one tile of R rows x BN columns: the larger of the
-// MMA time (R x BN x 64 MACs at 8192 FLOP per clock per SM) and the time to
-// move its (R + BN) operand rows of 128 bytes into shared memory at an
-// assumed ~64 B per clock per SM from L2.
-inline int64_t kblock_cycles(int64_t R, int64_t BN) {
-  const int64_t mma = R * BN / 64, traffic = 2 * (R + BN);
-  return mma > traffic ? mma : traffic;
-}
-
-// 256 x 256 tiles read (256 + 256) operand rows per K block for twice the
-// MMA work of a 128 x 256 tile's (128 + 256): a third less operand traffic
-// per FLOP.  Their two accumulators fill TMEM (no double buffering, so each
-// tile's epilogue is exposed, counted as 3 %), and they halve the tile
-// count.  Mode 1 takes them where rounds x cycles per K block come out
-// lower than for the 128-row tiles pick_bn would choose.
-bool use_tall_tiles(int64_t M, int64_t N, int sms) {
-  const int mode = g_gemm_rows.load(std::memory_order_relaxed);
-  if (mode == 0 || M <= tc::kBM) return false;
-  if (mode == 2) return true;
-  const int bn = pick_bn(M, N, sms);
-  const int64_t tiles = ((M + tc::kBM - 1) / tc::kBM) * ((N + bn - 1) / bn);
-  const int64_t cost = (tiles + sms - 1) / sms * kblock_cycles(tc::kBM, bn);
-  const int64_t tall_tiles = ((M + 2 * tc::kBM - 1) / (2 * tc::kBM)) * ((N + 255) / 256);
-  const int64_t tall_cost = (tall_tiles + sms - 1) / sms * kblock_cycles(2 * tc::kBM, 256) * 103 / 100;
-  return tall_cost < cost;
 }
 
 // ---------------------------------------------------------------- stream-K
@@ -383,19 +348,12 @@ int launch_gemm_tc(const void* A, const void* B, int ab_dtype, bool fp8, int64_t
   }
   int dev;
   if (int st = current_device(&dev)) return st;
-  const bool tall = use_tall_tiles(M, N, sm_count(dev));
-  const int bn = tall ? 256 : pick_bn(M, N, sm_count(dev));
+  const int bn = pick_bn(M, N, sm_count(dev));
   CUtensorMap ta, tb;
-  // the A box stays 128 rows: a tall tile loads its two row halves separately
   if (int st = make_kmajor_map(&ta, A, fp8, ab_dtype, M, K, tc::kBM)) return st;
   if (int st = make_kmajor_map(&tb, B, fp8, ab_dtype, N, K, bn)) return st;
   const int eb = fp8 ? 1 : 2;
   const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
-  if (tall) {
-    if (fp8) return launch_tc_inst<256, true, 0, 2>(ta, tb, (int)M, (int)N, num_kb, ep, s);
-    if (ab_dtype == MTP_DTYPE_BF16) return launch_tc_inst<256, false, 1, 2>(ta, tb, (int)M, (int)N, num_kb, ep, s);
-    return launch_tc_inst<256, false, 0, 2>(ta, tb, (int)M, (int)N, num_kb, ep, s);
-  }
   if (fp8) return launch_tc_bn<true, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
   if (ab_dtype == MTP_DTYPE_BF16) return launch_tc_bn<false, 1>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
   return launch_tc_bn<false, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
@@ -590,50 +548,38 @@ int mtp_set_gemm_schedule(int mode) {
 
 int mtp_gemm_schedule(void) { return g_gemm_schedule.load(std::memory_order_relaxed); }
 
-int mtp_set_gemm_tile_rows(int mode) {
-  if (mode < 0 || mode > 2) return fail(MTP_ERR_ARG, "GEMM tile-rows mode %d (expected 0, 1 or 2)", mode);
-  g_gemm_rows.store(mode, std::memory_order_relaxed);
-  return MTP_OK;
-}
-
-int mtp_gemm_tile_rows(void) { return g_gemm_rows.load(std::memory_order_relaxed); }
-
-int mtp_gemm_tile_check(int64_t M, int64_t N, int rows, int grid, int64_t* max_units) {
-  if (M <= 0 || N <= 0 || grid <= 0 || (rows != 128 && rows != 256) || M > INT32_MAX / 2 || N > INT32_MAX / 2)
+int mtp_gemm_tile_check(int64_t M, int64_t N, int grid, int64_t* max_tiles) {
+  if (M <= 0 || N <= 0 || grid <= 0 || M > INT32_MAX / 2 || N > INT32_MAX / 2)
     return fail(MTP_ERR_ARG, "bad tile-check arguments");
   const int bn = 256;
-  const int num_m = (int)((M + rows - 1) / rows), num_n = (int)((N + bn - 1) / bn);
+  const int num_m = (int)((M + tc::kBM - 1) / tc::kBM), num_n = (int)((N + bn - 1) / bn);
   const int64_t num_tiles = (int64_t)num_m * num_n;
   if (num_tiles > (1 << 26)) return fail(MTP_ERR_ARG, "too many tiles to check");
   std::vector<uint8_t> seen((size_t)num_tiles, 0);
   int64_t worst = 0;
   for (int c = 0; c < grid; ++c) {
-    int64_t units = 0;  // 128-row halves this CTA multiplies
-    for (int64_t t = c, j = 0; t < num_tiles; t += grid, ++j) {
+    int64_t tiles = 0;
+    for (int64_t t = c; t < num_tiles; t += grid) {
       int mb, nb;
-      if (rows == 256) tc::tile_coords<2>((int)t, (int)j, num_m, grid, mb, nb);
-      else tc::tile_coords<1>((int)t, (int)j, num_m, grid, mb, nb);
+      tc::tile_coords((int)t, num_m, mb, nb);
       if (mb < 0 || mb >= num_m || nb < 0 || nb >= num_n)
-        return fail(MTP_ERR_SHAPE, "CTA %d round %lld: tile (%d, %d) outside %d x %d", c, (long long)j, mb, nb,
-                    num_m, num_n);
+        return fail(MTP_ERR_SHAPE, "CTA %d: tile (%d, %d) outside %d x %d", c, mb, nb, num_m, num_n);
       uint8_t& s = seen[(size_t)nb * num_m + mb];
       if (s) return fail(MTP_ERR_SHAPE, "tile (%d, %d) taken twice", mb, nb);
       s = 1;
-      units += (rows == 256 && (int64_t)mb * 256 + 128 >= M) ? 1 : rows / 128;
+      ++tiles;
     }
-    worst = units > worst ? units : worst;
+    worst = tiles > worst ? tiles : worst;
   }
   for (int64_t i = 0; i < num_tiles; ++i)
     if (!seen[(size_t)i]) return fail(MTP_ERR_SHAPE, "tile %lld never taken", (long long)i);
-  if (max_units) *max_units = worst;
+  if (max_tiles) *max_tiles = worst;
   return MTP_OK;
 }
 
-int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* rows, int* bn) {
-  if (M <= 0 || N <= 0 || sms <= 0 || !rows || !bn) return fail(MTP_ERR_ARG, "bad tile-plan arguments");
-  const bool tall = use_tall_tiles(M, N, sms);
-  *rows = tall ? 2 * tc::kBM : tc::kBM;
-  *bn = tall ? 256 : pick_bn(M, N, sms);
+int mtp_gemm_tile_plan(int64_t M, int64_t N, int sms, int* bn) {
+  if (M <= 0 || N <= 0 || sms <= 0 || !bn) return fail(MTP_ERR_ARG, "bad tile-plan arguments");
+  *bn = pick_bn(M, N, sms);
   return MTP_OK;
 }
 
@@ -1153,10 +1099,9 @@ struct TreePlan {
   size_t ws_bytes = 256;
 };
 
-// chunk: keys per chunk of the kernel the plan is for (128 for
-// tree_attention_tc_kernel, 64 for tree_attention_tc2_kernel).
 TreePlan tree_plan(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t ctx_len, int64_t page_size,
-                   int64_t num_pages, int dtype, int chunk = attn::kChunk) {
+                   int64_t num_pages, int dtype) {
+  constexpr int chunk = attn::kChunk;
   TreePlan pl;
   if (!(dtype == MTP_DTYPE_BF16 || dtype == MTP_DTYPE_F16) || D != attn::kD || Hkv <= 0 || Hq % Hkv) return pl;
   const int64_t G = Hq / Hkv;
@@ -1212,24 +1157,6 @@ int make_map(CUtensorMap* map, const void* base, int dtype, int rank, const uint
   return MTP_OK;
 }
 
-// Tree-attention kernel: 1 = the 128-key kernel (default), 2 =
-// tree_attention_tc2_kernel (64-key chunks, double-buffered scores).  The
-// environment (MTP_ATTN_KERNEL=2) sets the initial choice; mtp_set_attn_kernel
-// changes it.
-std::atomic<int> g_attn_kernel{0};
-
-int attn_kernel_version() {
-  int v = g_attn_kernel.load(std::memory_order_relaxed);
-  if (v == 0) {
-    const char* e = getenv("MTP_ATTN_KERNEL");
-    v = (e && e[0] == '2' && e[1] == 0) ? 2 : 1;
-    int expected = 0;
-    g_attn_kernel.compare_exchange_strong(expected, v);
-    v = g_attn_kernel.load(std::memory_order_relaxed);
-  }
-  return v;
-}
-
 template <typename Kern>
 int set_smem_once(Kern kern, int bytes, bool* done, int dev) {
   if (!done[dev]) {
@@ -1243,8 +1170,8 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
                              const int32_t* page_table, int64_t table_stride, int64_t ctx_len, const void* tree_k,
                              const void* tree_v, const float* tree_mask, void* out, int dtype, int64_t B, int64_t T,
                              int64_t Hq, int64_t Hkv, int64_t num_pages, int64_t page_size, float scale,
-                             void* workspace, cudaStream_t s, int version) {
-  const int chunk = version == 2 ? attn2::kChunk : attn::kChunk;
+                             void* workspace, cudaStream_t s) {
+  const int chunk = attn::kChunk;
   const uint64_t D = attn::kD, E = 2;
   CUtensorMap tq, tk, tv, ttk, ttv;
   {
@@ -1303,16 +1230,8 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
   int dev;
   if (int st = current_device(&dev)) return st;
   const int grid = (int)(B * Hkv * pl.splits);
-  static bool attr[4][kMaxDevices] = {};
-  if (version == 2) {
-    if (dtype == MTP_DTYPE_BF16) {
-      if (int st = set_smem_once(attn2::tree_attention_tc2_kernel<1>, attn2::kSmemBytes, attr[2], dev)) return st;
-      attn2::tree_attention_tc2_kernel<1><<<grid, attn2::kThreads, attn2::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
-    } else {
-      if (int st = set_smem_once(attn2::tree_attention_tc2_kernel<0>, attn2::kSmemBytes, attr[3], dev)) return st;
-      attn2::tree_attention_tc2_kernel<0><<<grid, attn2::kThreads, attn2::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
-    }
-  } else if (dtype == MTP_DTYPE_BF16) {
+  static bool attr[2][kMaxDevices] = {};
+  if (dtype == MTP_DTYPE_BF16) {
     if (int st = set_smem_once(attn::tree_attention_tc_kernel<1>, attn::kSmemBytes, attr[0], dev)) return st;
     attn::tree_attention_tc_kernel<1><<<grid, attn::kThreads, attn::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);
   } else {
@@ -1332,14 +1251,6 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
 
 extern "C" {
 
-int mtp_set_attn_kernel(int version) {
-  if (version != 1 && version != 2) return fail(MTP_ERR_ARG, "attention kernel %d (expected 1 or 2)", version);
-  g_attn_kernel.store(version, std::memory_order_relaxed);
-  return MTP_OK;
-}
-
-int mtp_attn_kernel(void) { return attn_kernel_version(); }
-
 int mtp_set_decode_kernel(int version) {
   if (version != 1 && version != 2) return fail(MTP_ERR_ARG, "decode kernel %d (expected 1 or 2)", version);
   g_decode_kernel.store(version, std::memory_order_relaxed);
@@ -1351,10 +1262,8 @@ int mtp_decode_kernel(void) { return decode_kernel_version(); }
 size_t mtp_tree_attention_paged_workspace(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
                                           int64_t ctx_len) {
   // page_size 16 / bf16 give the same plan as every other eligible case of
-  // these sizes; the larger of the two kernels' needs
-  const TreePlan p1 = tree_plan(B, T, Hq, Hkv, D, ctx_len, 16, 1, MTP_DTYPE_BF16, attn::kChunk);
-  const TreePlan p2 = tree_plan(B, T, Hq, Hkv, D, ctx_len, 16, 1, MTP_DTYPE_BF16, attn2::kChunk);
-  return p1.ws_bytes > p2.ws_bytes ? p1.ws_bytes : p2.ws_bytes;
+  // these sizes
+  return tree_plan(B, T, Hq, Hkv, D, ctx_len, 16, 1, MTP_DTYPE_BF16).ws_bytes;
 }
 
 int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_pages, const int32_t* page_table,
@@ -1371,13 +1280,7 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
   if (B * T == 0) return MTP_OK;
   if (!q || !out || !tree_k || !tree_v || !tree_mask || (ctx_len > 0 && (!k_pages || !v_pages || !page_table)))
     return fail(MTP_ERR_ARG, "null tensor pointer");
-  int version = attn_kernel_version();
-  TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype,
-                          version == 2 ? attn2::kChunk : attn::kChunk);
-  if (version == 2 && !pl.eligible) {  // e.g. 128-token pages: the 128-key kernel takes them
-    version = 1;
-    pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype, attn::kChunk);
-  }
+  const TreePlan pl = tree_plan(B, T, Hq, Hkv, D, ctx_len, page_size, num_pages, dtype);
   const bool aligned = aligned16(q) && aligned16(out) && aligned16(tree_k) && aligned16(tree_v) &&
                        (ctx_len == 0 || (aligned16(k_pages) && aligned16(v_pages)));
   if (pl.eligible && aligned && scale > 0.f) {  // the kernel folds a positive scale into exp2
@@ -1385,7 +1288,7 @@ int mtp_tree_attention_paged(const void* q, const void* k_pages, const void* v_p
       return fail(MTP_ERR_WORKSPACE, "workspace of %zu bytes needed", pl.ws_bytes);
     return launch_tree_attention_tc(pl, q, k_pages, v_pages, page_table, table_stride, ctx_len, tree_k, tree_v,
                                     tree_mask, out, dtype, B, T, Hq, Hkv, num_pages, page_size, scale, workspace,
-                                    as_stream(stream), version);
+                                    as_stream(stream));
   }
   AttnArgs a{};
   a.kind = ATTN_TREE_PAGED;

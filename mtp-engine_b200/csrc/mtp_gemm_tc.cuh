@@ -32,27 +32,22 @@ constexpr int kBM = 128;
 constexpr int kThreads = 192;
 constexpr int kKBlockBytes = 128;  // one 128-byte swizzle row of K per stage
 
-// MH = row halves per tile: 1 -> 128 x BN tiles; 2 -> 256 x BN tiles, two
-// M=128 MMAs per K step sharing one B (weight) stage, which cuts the operand
-// traffic per FLOP from (128 + BN) / (128 BN) to (256 + BN) / (256 BN) rows.
-template <int BN, int MH = 1>
+template <int BN>
 struct Cfg {
-  static constexpr int TILE_M = MH * kBM;
-  static constexpr int HALF_BYTES = kBM * kKBlockBytes;  // one 128-row half of an A stage
-  static constexpr int A_BYTES = MH * HALF_BYTES;
+  static constexpr int TILE_M = kBM;
+  static constexpr int A_BYTES = kBM * kKBlockBytes;
   static constexpr int B_BYTES = BN * kKBlockBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (220 * 1024 / STAGE_BYTES) < 8 ? (220 * 1024 / STAGE_BYTES) : 8;
-  static constexpr int ACC_COLS = MH * BN;                        // one tile's accumulators
-  static constexpr int ACC_BUFS = (2 * ACC_COLS <= 512) ? 2 : 1;  // double-buffered when two fit
+  static constexpr int ACC_COLS = BN;  // one tile's accumulators
+  static constexpr int ACC_BUFS = 2;   // double-buffered: tile i's epilogue overlaps tile i+1's mainloop
   static constexpr int TMEM_COLS = (ACC_BUFS * ACC_COLS <= 256) ? 256 : 512;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  static_assert(MH == 1 || MH == 2, "one or two row halves");
   // UMMA with M = 128: N a multiple of 16 in [16, 256]
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tile width");
   // SW128 operand atoms are 8 rows x 128 bytes; every stage base stays 1024-byte aligned
-  static_assert(HALF_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage alignment");
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage alignment");
   static_assert(STAGES >= 2, "at least a double-buffered ring");
   // full/empty per stage, tfull/tempty x2, drain; then the TMEM slot and four flags (stream-K uses all)
   static_assert((2 * STAGES + 5) * 8 + 5 * 4 <= BAR_BYTES, "barrier area");
@@ -60,19 +55,13 @@ struct Cfg {
   static_assert(ACC_BUFS * ACC_COLS <= TMEM_COLS && TMEM_COLS <= 512, "accumulators in TMEM");
 };
 
-// Tile t, taken by a CTA in round j (t = blockIdx.x + j * gridDim.x) -> row
-// tile mb and column tile nb, M-fastest so the CTAs that share a weight tile
-// run at the same time.  With 256-row tiles the last row tile is often half
-// empty (384 verify rows = 256 + 128); when the grid is a multiple of num_m
-// the plain order would give each CTA the same row tile in every round, so
-// the row tile is rotated by the round instead -- still a permutation of the
-// tiles of each round, and every CTA sees every row tile in turn.
-// Host and device run the same code (the host to check the order).
-template <int MH>
-__host__ __device__ __forceinline__ void tile_coords(int t, int j, int num_m, int grid, int& mb, int& nb) {
+// Tile t (taken by a CTA as t = blockIdx.x + j * gridDim.x) -> row tile mb
+// and column tile nb, M-fastest so the CTAs that share a weight tile run at
+// the same time.  Host and device run the same code (the host to check the
+// order).
+__host__ __device__ __forceinline__ void tile_coords(int t, int num_m, int& mb, int& nb) {
   nb = t / num_m;
-  if (MH == 2 && grid % num_m == 0) mb = (t + j) % num_m;
-  else mb = t % num_m;
+  mb = t % num_m;
 }
 
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -145,11 +134,11 @@ __device__ __forceinline__ void tmem_ld32_f(uint32_t taddr, float (&v)[32]) {
 }
 
 // ab_fmt: 0 = f16, 1 = bf16 (kind::f16); FP8: E4M3 x E4M3 (kind::f8f6f4)
-template <int BN, bool FP8, int AB_FMT, int MH = 1>
+template <int BN, bool FP8, int AB_FMT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                    int N, int num_kb, GemmEpilogue ep) {
-  using C = Cfg<BN, MH>;
+  using C = Cfg<BN>;
   constexpr int KB_ELEMS = FP8 ? 128 : 64;       // elements per 128-byte K block
   constexpr int UMMA_K_BYTES = 32;               // K per tcgen05.mma: 16 x 16-bit or 32 x 8-bit
   constexpr int K_STEPS = kKBlockBytes / UMMA_K_BYTES;
@@ -199,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_m = (M + C::TILE_M - 1) / C::TILE_M;
+  const int num_m = (M + kBM - 1) / kBM;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
 
@@ -209,20 +198,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x, j = 0; t < num_tiles && ok; t += gridDim.x, ++j) {
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mb, nb;
-        tile_coords<MH>(t, j, num_m, (int)gridDim.x, mb, nb);
-        // a row half that lies wholly past M is neither loaded nor multiplied
-        const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
+        tile_coords(t, num_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[stage], halves * C::HALF_BYTES + C::B_BYTES);
-          for (int h = 0; h < halves; ++h)
-            tma_load_2d(sA + stage * C::A_BYTES + h * C::HALF_BYTES, &tmA, kb * KB_ELEMS, mb * C::TILE_M + h * kBM,
-                        &full[stage]);
+          mbar_expect_tx(&full[stage], C::A_BYTES + C::B_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, kb * KB_ELEMS, mb * kBM, &full[stage]);
           tma_load_2d(sB + stage * C::B_BYTES, &tmB, kb * KB_ELEMS, nb * BN, &full[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -239,11 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int local = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-        int mb, nb;
-        tile_coords<MH>(t, local, num_m, (int)gridDim.x, mb, nb);
-        const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
-        const int acc = C::ACC_BUFS == 2 ? (local & 1) : 0;
-        const uint32_t acc_phase = C::ACC_BUFS == 2 ? ((local >> 1) & 1) : (local & 1);
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
           ok = false;
           break;
@@ -260,15 +242,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < K_STEPS; ++k) {
+            const uint64_t ad = sw128_kmajor_desc(a_addr + k * UMMA_K_BYTES);
             const uint64_t bd = sw128_kmajor_desc(b_addr + k * UMMA_K_BYTES);
-#pragma unroll
-            for (int h = 0; h < MH; ++h) {
-              if (h >= halves) break;
-              // half h: rows h*128.. of the tile, accumulator columns h*BN..
-              const uint64_t ad = sw128_kmajor_desc(a_addr + h * C::HALF_BYTES + k * UMMA_K_BYTES);
-              if constexpr (FP8) umma_f8(d_tmem + (uint32_t)(h * BN), ad, bd, IDESC, (kb | k) != 0);
-              else umma_f16(d_tmem + (uint32_t)(h * BN), ad, bd, IDESC, (kb | k) != 0);
-            }
+            if constexpr (FP8) umma_f8(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+            else umma_f16(d_tmem, ad, bd, IDESC, (kb | k) != 0);
           }
           umma_commit(&empty[stage]);  // frees this stage once its MMAs have read it
           if (++stage == C::STAGES) {
@@ -290,19 +267,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int mb, nb;
-      tile_coords<MH>(t, local, num_m, (int)gridDim.x, mb, nb);
-      const int halves = (MH == 2 && mb * C::TILE_M + kBM >= M) ? 1 : MH;
-      const int acc = C::ACC_BUFS == 2 ? (local & 1) : 0;
-      const uint32_t acc_phase = C::ACC_BUFS == 2 ? ((local >> 1) & 1) : (local & 1);
+      tile_coords(t, num_m, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
       const bool got = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int h = 0; h < halves; ++h) {
-        const int row = mb * C::TILE_M + h * kBM + row_in_tile;
+      {
+        const int row = mb * kBM + row_in_tile;
         const bool row_ok = row < M;
-        const uint32_t tbase =
-            tmem_base + (uint32_t)(acc * C::ACC_COLS + h * BN) + ((uint32_t)(q * 32) << 16);
+        const uint32_t tbase = tmem_base + (uint32_t)(acc * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
         if (ep.mode == EPI_STORE) {
           const float rs = (ep.row_scale && row_ok) ? ep.row_scale[row] : 1.0f;
 #pragma unroll 1
@@ -323,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (row_ok) atomicMax(&ep.keys[row], make_key(best, (uint32_t)(ep.col_offset + best_n)));
         }
-      }  // row halves
+      }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }

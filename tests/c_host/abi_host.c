@@ -23,15 +23,12 @@ int main(void) {
   /* schedule and kernel switches */
   CHECK(mtp_set_gemm_schedule(2) == MTP_ERR_ARG);
   CHECK(strlen(mtp_last_error()) > 0);
-  CHECK(mtp_set_gemm_tile_rows(1) == MTP_OK && mtp_gemm_tile_rows() == 1);
-  int rows = 0, bn = 0;
-  CHECK(mtp_gemm_tile_plan(384, 128256, 148, &rows, &bn) == MTP_OK && rows == 256 && bn == 256);
-  CHECK(mtp_set_gemm_tile_rows(0) == MTP_OK);
-  CHECK(mtp_gemm_tile_plan(384, 128256, 148, &rows, &bn) == MTP_OK && rows == 128);
+  int bn = 0;
+  CHECK(mtp_gemm_tile_plan(384, 128256, 148, &bn) == MTP_OK && bn == 256);
 
   /* host walks of the kernels' own schedules */
-  int64_t units = 0;
-  CHECK(mtp_gemm_tile_check(384, 128256, 256, 148, &units) == MTP_OK && units == 11);
+  int64_t tiles = 0;
+  CHECK(mtp_gemm_tile_check(384, 128256, 148, &tiles) == MTP_OK && tiles == 11);
   CHECK(mtp_gemm_streamk_check(384, 128256, 4096, MTP_DTYPE_BF16, 148, 0) == MTP_OK);
   int64_t info[9];
   CHECK(mtp_gemm_streamk_plan(384, 128256, 4096, MTP_DTYPE_BF16, 148, 0, info) == MTP_OK && info[0] == 1);

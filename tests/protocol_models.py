@@ -1,4 +1,4 @@
-"""Randomised interleaving models of two synchronisation protocols, used by
+"""Randomised interleaving models of synchronisation protocols, used by
 tests/test_protocol_models.py (test infrastructure, CPU only).
 
 Each kernel role is a Python generator; the asynchronous engines (TMA copy
@@ -10,14 +10,11 @@ that passes early or a read of stale data raises Violation.
 
 import random
 
-# --------------------------------------------------------------------------- #
-# tree_attention_tc2_kernel (csrc/mtp_attention_tc2.cuh): TMA producer, MMA
-# issuer and softmax warps over the K/V ring, the two score buffers per query
-# tile (S/P tags) and the O accumulator (set of chunks it holds)
-# --------------------------------------------------------------------------- #
-
 
 class Bar:
+    """An mbarrier: `count` arrivals plus outstanding transaction bytes
+    complete a phase; test(parity) is try_wait.parity."""
+
     def __init__(self, name, count):
         self.name, self.count, self.pending, self.done = name, count, count, 0
         self.tx = 0
@@ -46,198 +43,6 @@ class Bar:
 
 class Violation(Exception):
     pass
-
-
-def run_attn2(seed, n_iter, n_tiles, kNumBuf=9, p_rescale=0.3, final_wait="o_done"):
-    rnd = random.Random(seed)
-    bars = {}
-
-    def B(name, count=1):
-        if name not in bars:
-            bars[name] = Bar(name, count)
-        return bars[name]
-
-    for i in range(kNumBuf):
-        B(f"buf_full{i}"), B(f"buf_empty{i}")
-    for t in range(n_tiles):
-        for sb in range(2):
-            B(f"s_full{t}{sb}"), B(f"p_full{t}{sb}", 4)
-        B(f"pv_done{t}"), B(f"o_done{t}")
-    B("q_full")
-
-    # state with tags
-    smem = [None] * kNumBuf          # item loaded in ring slot
-    S = {(t, sb): None for t in range(n_tiles) for sb in range(2)}  # ('S', c) or ('P', c)
-    O = {t: set() for t in range(n_tiles)}   # chunks accumulated
-    O_scaled_at = {t: [] for t in range(n_tiles)}
-    tma_q = []     # pending TMA completions: (slot, item)
-    pipe = []      # in-order tcgen05 ops: ('S', t, sb, item, c) | ('PV', t, sb, item, c) | ('commit', bar)
-    results = {}
-
-    def wait(bar, parity, want_done):
-        """yield until bar passes parity; check it passed for the intended completion."""
-        while not bars[bar].test(parity):
-            yield "blocked"
-        if bars[bar].done < want_done:
-            raise Violation(f"{bar}: parity {parity} passed with {bars[bar].done} completions, wanted {want_done}")
-
-    # ------------------------------------------------------------ producer
-    def producer():
-        # Q
-        bars["q_full"].expect_tx(1)
-        tma_q.append(("Q", None))
-        item = 0
-        for c in range(n_iter):
-            for kv in range(2):
-                buf = item % kNumBuf
-                yield from wait(f"buf_empty{buf}", ((item // kNumBuf) & 1) ^ 1, item // kNumBuf)
-                if smem[buf] is not None and smem[buf][1] is False:
-                    raise Violation(f"producer overwrites slot {buf} holding unconsumed item {smem[buf]}")
-                bars[f"buf_full{buf}"].expect_tx(1)
-                tma_q.append((buf, item))
-                item += 1
-                yield "step"
-
-    # ------------------------------------------------------------ MMA issuer
-    def mma():
-        yield from wait("q_full", 0, 1)
-
-        def wait_item(it):
-            yield from wait(f"buf_full{it % kNumBuf}", (it // kNumBuf) & 1, it // kNumBuf + 1)
-
-        for j in range(min(2, n_iter)):
-            yield from wait_item(2 * j)
-            for t in range(n_tiles):
-                pipe.append(("S", t, j, 2 * j, j))
-                pipe.append(("commit", f"s_full{t}{j}"))
-            pipe.append(("consumed", 2 * j))
-            pipe.append(("commit", f"buf_empty{(2 * j) % kNumBuf}"))
-            yield "step"
-        for i in range(n_iter):
-            sb = i & 1
-            vitem, knext = 2 * i + 1, 2 * i + 4
-            for t in range(n_tiles):
-                yield from wait(f"p_full{t}{sb}", (i >> 1) & 1, (i >> 1) + 1)
-                if t == 0:
-                    yield from wait_item(vitem)
-                pipe.append(("PV", t, sb, vitem, i))
-                pipe.append(("commit", f"pv_done{t}"))
-                if i == n_iter - 1:
-                    pipe.append(("commit", f"o_done{t}"))
-                if t == n_tiles - 1:
-                    pipe.append(("consumed", vitem))
-                    pipe.append(("commit", f"buf_empty{vitem % kNumBuf}"))
-                if i + 2 < n_iter:
-                    if t == 0:
-                        yield from wait_item(knext)
-                    pipe.append(("S", t, sb, knext, i + 2))
-                    pipe.append(("commit", f"s_full{t}{sb}"))
-                    if t == n_tiles - 1:
-                        pipe.append(("consumed", knext))
-                        pipe.append(("commit", f"buf_empty{knext % kNumBuf}"))
-                yield "step"
-
-    # ------------------------------------------------------------ softmax warp
-    def softmax(t, w):
-        for i in range(n_iter):
-            sb = i & 1
-            yield from wait(f"s_full{t}{sb}", (i >> 1) & 1, (i >> 1) + 1)
-            if S[(t, sb)] != ("S", i):
-                raise Violation(f"softmax t{t} w{w} chunk {i} reads {S[(t, sb)]}")
-            yield "step"  # compute
-            if i > 0 and rnd.random() < p_rescale:
-                yield from wait(f"pv_done{t}", (i - 1) & 1, i)
-                if O[t] != set(range(i)):
-                    raise Violation(f"rescale t{t} chunk {i}: O holds {sorted(O[t])}")
-                yield "step"
-                if O[t] != set(range(i)):
-                    raise Violation(f"rescale t{t} chunk {i} (store): O holds {sorted(O[t])}")
-            # write P (one warp's quarter: model as the whole buffer once all 4 warps wrote)
-            key = (t, sb, i)
-            results.setdefault(key, 0)
-            results[key] += 1
-            if results[key] == 4:
-                if S[(t, sb)] != ("S", i):
-                    raise Violation(f"P write t{t} chunk {i} over {S[(t, sb)]}")
-                S[(t, sb)] = ("P", i)
-            bars[f"p_full{t}{sb}"].arrive()
-            yield "step"
-        if final_wait == "o_done":
-            yield from wait(f"o_done{t}", 0, 1)
-        else:  # control: a parity wait on the per-PV barrier
-            yield from wait(f"pv_done{t}", (n_iter - 1) & 1, n_iter)
-        if O[t] != set(range(n_iter)):
-            raise Violation(f"final O t{t} holds {sorted(O[t])}")
-
-    roles = [producer(), mma()] + [softmax(t, w) for t in range(n_tiles) for w in range(4)]
-    alive = list(roles)
-
-    def engine_steps():
-        acts = []
-        if tma_q:
-            acts.append("tma")
-        if pipe:
-            acts.append("pipe")
-        return acts
-
-    steps = 0
-    blocked_rounds = 0
-    while alive or tma_q or pipe:
-        steps += 1
-        if steps > 200000:
-            raise Violation("no progress (livelock)")
-        choices = [("role", r) for r in alive] + [("eng", e) for e in engine_steps()]
-        kind, what = rnd.choice(choices)
-        if kind == "role":
-            try:
-                st = next(what)
-            except StopIteration:
-                alive.remove(what)
-                blocked_rounds = 0
-                continue
-            if st == "blocked":
-                blocked_rounds += 1
-                if blocked_rounds > 5000 and not tma_q and not pipe:
-                    raise Violation("deadlock: " + ", ".join(f"{b.name}:{b.done}" for b in bars.values()))
-            else:
-                blocked_rounds = 0
-        elif what == "tma":
-            k = rnd.randrange(len(tma_q))
-            slot, item = tma_q.pop(k)
-            if slot == "Q":
-                bars["q_full"].complete_tx(1)
-            else:
-                smem[slot] = (item, False)
-                bars[f"buf_full{slot}"].complete_tx(1)
-            blocked_rounds = 0
-        else:
-            op = pipe.pop(0)
-            blocked_rounds = 0
-            if op[0] == "commit":
-                bars[op[1]].arrive()
-            elif op[0] == "consumed":
-                it = op[1]
-                slot = it % kNumBuf
-                if smem[slot] is None or smem[slot][0] != it:
-                    raise Violation(f"consumed item {it} but slot holds {smem[slot]}")
-                smem[slot] = (it, True)
-            else:
-                kindop, t, sb, item, c = op
-                slot = item % kNumBuf
-                if smem[slot] is None or smem[slot][0] != item:
-                    raise Violation(f"{kindop} t{t} chunk {c} reads slot {slot} holding {smem[slot]}, want {item}")
-                if kindop == "S":
-                    if S[(t, sb)] is not None and S[(t, sb)] != ("P", c - 2):
-                        raise Violation(f"S t{t} chunk {c} overwrites {S[(t, sb)]}")
-                    S[(t, sb)] = ("S", c)
-                else:
-                    if S[(t, sb)] != ("P", c):
-                        raise Violation(f"PV t{t} chunk {c} reads {S[(t, sb)]}")
-                    O[t].add(c)
-    return steps
-
-
-
 
 # --------------------------------------------------------------------------- #
 # verify_exchange_chain_kernel (csrc/mtp_verify.cuh).  Each rank runs E calls.

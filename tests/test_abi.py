@@ -27,7 +27,7 @@ def test_library_exports_all():
     lib = N.lib()
     for name in header_functions():
         assert hasattr(lib, name), name
-    assert lib.mtp_abi_version() == 1
+    assert lib.mtp_abi_version() == 2
 
 
 def test_workspace_sizes():
@@ -75,20 +75,6 @@ def test_out_of_scope_names():
     with pytest.raises(AttributeError, match="not part of the B200 hot path"):
         mtp_kernels.fused_causal_attention_autotuned  # noqa: B018
     assert mtp_kernels._HAS_TRITON is False
-
-
-def test_attn_kernel_switch_roundtrip():
-    import _mtp_native as N
-    before = N.attn_kernel()
-    assert before in (1, 2)
-    try:
-        N.set_attn_kernel(2)
-        assert N.attn_kernel() == 2
-        N.set_attn_kernel(1)
-        assert N.attn_kernel() == 1
-        assert N.lib().mtp_set_attn_kernel(3) == 8  # MTP_ERR_ARG
-    finally:
-        N.set_attn_kernel(before)
 
 
 def test_new_entry_points_checks_without_launch():

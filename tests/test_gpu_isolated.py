@@ -1,6 +1,5 @@
 """Runs the GPU tests marked `isolated` -- each group of files in its own
-child pytest process -- plus the tree-attention tests under the opt-in
-64-key kernel (MTP_ATTN_KERNEL=2).  A fault in one of them then cannot leave
+child pytest process.  A fault in one of them then cannot leave
 this process's CUDA context unusable for the tests after it.  Every child
 must pass: a failing child fails this test, and its failing test ids are
 printed on one line (`FAILED-IN-CHILD <name>: id, id, ...`) so they survive
@@ -21,13 +20,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 # name -> (test files, extra environment, -k expression)
 CHILDREN = {
     "streamk": (["test_gpu_streamk.py"], {}, None),
-    "tall_tiles": (["test_gpu_tall_tiles.py"], {}, None),
     "tree_attn_rmsnorm_linear": (["test_gpu_tree_attn_rmsnorm_linear.py"], {}, None),
     "nccl_abi": (["test_gpu_nccl_abi.py"], {"NCCL_NVLS_ENABLE": "0"}, None),
     "exchange_single_gpu": (["test_gpu_exchange_single.py"], {}, None),
     "edge_shapes": (["test_gpu_edge_shapes.py"], {}, None),
-    "attention_64key_kernel": (["test_gpu_attention_tc.py", "test_gpu_parity.py"], {"MTP_ATTN_KERNEL": "2"},
-                               "attention or edge_cases or device_status"),
     "verify_step": (["test_verify_step.py"], {}, None),
     "paged_kv_write": (["test_paged_kv_write.py"], {}, None),
     "quant_attention_int4": (["test_quant_attention_int4.py"], {}, None),

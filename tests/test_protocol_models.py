@@ -1,10 +1,9 @@
-"""The synchronisation protocols of kernels that have not yet run on a
-GPU, checked on the CPU with randomised interleaving models
-(tests/protocol_models.py): the 64-key tree attention's mbarrier protocol,
-the vocab-parallel peer-memory key exchange, the exchange fused into the
-shard GEMM, and the GEMM's accumulator handshake with one or two buffers.  Each model must be clean
-for the protocol the kernel uses and must catch a known-bad variant (the
-previous final wait of the attention kernel; one parity for the exchange),
+"""Synchronisation protocols of the kernels, checked on the CPU with
+randomised interleaving models (tests/protocol_models.py): the
+vocab-parallel peer-memory key exchange, the exchange fused into the shard
+GEMM, and the GEMM's accumulator handshake.  Each model must be clean for
+the protocol the kernel uses and must catch a known-bad variant (one parity
+for the exchange; the double-buffer phase formula on a single accumulator),
 which shows the model can see the bug it guards against."""
 
 import pytest
@@ -22,16 +21,6 @@ def _count(fn, seeds):
     return bad
 
 
-def _attn(final_wait):
-    return lambda seed: PM.run_attn2(seed, 1 + seed % 11, 1 + (seed // 11) % 2,
-                                     p_rescale=(0.0, 0.3, 1.0)[seed % 3], final_wait=final_wait)
-
-
-def test_attention_tc2_protocol():
-    assert _count(_attn("o_done"), range(400)) == 0
-    assert _count(_attn("pv_parity"), range(400)) > 0
-
-
 def test_exchange_protocol():
     run = lambda par: (lambda seed: PM.run_exchange(seed, 2 + seed % 7, 6, parities=par))
     assert _count(run(2), range(300)) == 0
@@ -46,9 +35,10 @@ def test_fused_exchange_protocol():
 
 @pytest.mark.parametrize("acc_bufs", [1, 2])
 def test_gemm_accumulator_handshake(acc_bufs):
-    """gemm_tc_kernel: double-buffered accumulators (128-row tiles) and the
-    single accumulator of the 256-row tiles -- every MMA reads the stage it
-    expects and the epilogue reads each tile's complete accumulator."""
+    """gemm_tc_kernel's double-buffered accumulators (and, as a second case
+    of the same handshake, a single accumulator with its own phase rule):
+    every MMA reads the stage it expects and the epilogue reads each tile's
+    complete accumulator."""
     for seed in range(150):
         PM.run_gemm(seed, n_tiles=7, num_kb=5, stages=3, acc_bufs=acc_bufs)
         PM.run_gemm(seed + 1000, n_tiles=4, num_kb=1, stages=2, acc_bufs=acc_bufs)

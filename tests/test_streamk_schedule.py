@@ -113,67 +113,35 @@ def test_whole_tile_plan_covers_every_block_once(M, Nn, K, dt):
     check(M, Nn, K, dt, grid=-1)
 
 
-def test_tile_rows_switch_roundtrip():
-    """The 256-row tile switch (no device needed to set it)."""
-    L = N.lib()
-    before = L.mtp_gemm_tile_rows()
-    assert before in (0, 1, 2)
-    try:
-        for m in (0, 1, 2):
-            N.set_gemm_tile_rows(m)
-            assert L.mtp_gemm_tile_rows() == m == N.gemm_tile_rows()
-        assert L.mtp_set_gemm_tile_rows(-1) == 8 and L.mtp_set_gemm_tile_rows(3) == 8  # MTP_ERR_ARG
-    finally:
-        N.set_gemm_tile_rows(before)
-
-
 def tile_plan(M, Nn, sms=SMS):
-    rows, bn = ctypes.c_int(0), ctypes.c_int(0)
-    N.check(N.lib().mtp_gemm_tile_plan(M, Nn, sms, ctypes.byref(rows), ctypes.byref(bn)), "mtp_gemm_tile_plan")
-    return rows.value, bn.value
+    bn = ctypes.c_int(0)
+    N.check(N.lib().mtp_gemm_tile_plan(M, Nn, sms, ctypes.byref(bn)), "mtp_gemm_tile_plan")
+    return bn.value
 
 
 def test_tile_plan_choices():
-    """Which workloads the cost model sends to 256 x 256 tiles (mode 1)."""
-    before = N.gemm_tile_rows()
-    try:
-        N.set_gemm_tile_rows(0)
-        assert tile_plan(384, 128256) == (128, 256) and tile_plan(512, 14336)[0] == 128
-        N.set_gemm_tile_rows(1)
-        assert tile_plan(384, 128256) == (256, 256)   # config 5, 1 GPU: 7 rounds instead of 11
-        assert tile_plan(384, 16032) == (256, 256)    # config 5, 1 of 8 ranks: 1 round instead of 2
-        assert tile_plan(512, 14336) == (256, 256)    # config 2, 1 GPU: 112 tiles in one round
-        assert tile_plan(512, 1792)[0] == 128         # config 2, 1 of 8 ranks: 28 tiles fit one round
-        assert tile_plan(64, 128256)[0] == 128        # one row half only
-        assert tile_plan(128, 100000)[0] == 128
-        N.set_gemm_tile_rows(2)
-        assert tile_plan(129, 64) == (256, 256) and tile_plan(128, 64)[0] == 128
-    finally:
-        N.set_gemm_tile_rows(before)
+    """The tile width chosen per problem (fewest rounds x (128 + BN) operand
+    rows per K block): config 5 verify 256, config 2 224."""
+    assert tile_plan(384, 128256) == 256
+    assert tile_plan(512, 14336) == 224
+    assert tile_plan(64, 100) == 64   # N <= 128: the narrowest tile
 
 
-def tile_check(M, Nn, rows, grid):
-    units = ctypes.c_int64(0)
-    st = N.lib().mtp_gemm_tile_check(M, Nn, rows, grid, ctypes.byref(units))
+def tile_check(M, Nn, grid):
+    tiles = ctypes.c_int64(0)
+    st = N.lib().mtp_gemm_tile_check(M, Nn, grid, ctypes.byref(tiles))
     assert st == 0, N.lib().mtp_last_error().decode()
-    return units.value
+    return tiles.value
 
 
 @pytest.mark.parametrize("M,Nn", [(384, 128256), (384, 16032), (512, 14336), (300, 1000), (129, 64),
                                   (1000, 70000), (256, 256), (640, 9000)])
 @pytest.mark.parametrize("grid", [1, 2, 3, 7, 74, 148, 149])
 def test_tile_order_covers_every_tile_once(M, Nn, grid):
-    for rows in (128, 256):
-        tile_check(M, Nn, rows, grid)
+    tile_check(M, Nn, grid)
 
 
-def test_tall_tile_rotation_balances_half_tiles():
-    """384 rows = one full and one half row tile per weight tile: on 148
-    CTAs the rotated order gives every CTA both in turn, so no CTA carries
-    more than its share (the plain order would give the even CTAs every full
-    tile: 2 units per round instead of 1.5)."""
-    tiles = 2 * -(-128256 // 256)          # 1002 tiles of 256 x 256
-    rounds = -(-tiles // SMS)              # 7
-    worst = tile_check(384, 128256, 256, SMS)
-    assert worst <= (rounds // 2 + 1) * 2 + (rounds // 2)  # 4 full + 3 half = 11 units
-    assert worst < 2 * rounds                               # below the unrotated 14
+def test_tile_order_balances_rounds():
+    """1503 tiles of 128 x 256 (config 5) on 148 CTAs: 11 rounds, no CTA
+    takes more than that."""
+    assert tile_check(384, 128256, SMS) == -(-(3 * -(-128256 // 256)) // SMS)
