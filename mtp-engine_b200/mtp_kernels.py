@@ -62,16 +62,17 @@ if torch.cuda.is_available():
 
 @dataclass(frozen=True)
 class KernelTuningConfig:
-    """Kept for API compatibility (mtp_kernels.py:54-62).  Tiling of the
-    sm_100a kernels is fixed at compile time; only ``fp8_scale`` is read (the
-    default ``scale`` of fused_rmsnorm_linear, mtp_kernels.py:943-944)."""
+    """Kept for API compatibility, with the reference's fields and defaults
+    (mtp_kernels.py:54-62).  Tiling of the sm_100a kernels is fixed at
+    compile time; only ``fp8_scale`` is read (the default ``scale`` of
+    fused_rmsnorm_linear, mtp_kernels.py:943-944)."""
 
-    BLOCK_M: int = 128
-    BLOCK_N: int = 256
-    BLOCK_K: int = 64
-    BLOCK_DHEAD: int = 128
-    num_warps: int = 6
-    num_stages: int = 4
+    BLOCK_M: int = 64
+    BLOCK_N: int = 64
+    BLOCK_K: int = 32
+    BLOCK_DHEAD: int = 64
+    num_warps: int = 4
+    num_stages: int = 2
     fp8_scale: float = 1.0
 
 
@@ -79,6 +80,16 @@ TUNING = KernelTuningConfig()
 
 
 def build_tuning_config() -> KernelTuningConfig:
+    """The values the reference's build_tuning_config returns for the
+    current device (mtp_kernels.py:91-103); informational only here."""
+    if torch.cuda.is_available():
+        major = torch.cuda.get_device_capability(0)[0]
+        if major >= 9:
+            return KernelTuningConfig(BLOCK_M=128, BLOCK_N=128, BLOCK_K=64, BLOCK_DHEAD=128, num_warps=8,
+                                      num_stages=3)
+        if major == 8:
+            return KernelTuningConfig(BLOCK_M=128, BLOCK_N=64, BLOCK_K=32, BLOCK_DHEAD=64, num_warps=4,
+                                      num_stages=2)
     return KernelTuningConfig()
 
 

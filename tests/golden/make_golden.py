@@ -82,6 +82,9 @@ def main():
         import mtp_engine
         make_paged_kv_write(torch, mtp_engine)
         return
+    if args.only == "api_signatures":
+        make_api_signatures()
+        return
     if args.only == "tree_paged_reserve":
         import mtp_engine
         make_tree_paged_reserve(torch, mk, mtp_engine)
@@ -285,6 +288,7 @@ def main():
     make_paged_kv_write(torch, mtp_engine)
     make_tree_paged_reserve(torch, mk, mtp_engine)
     make_quant_attention_int4(torch, mk)
+    make_api_signatures()
 
 
 # (depth, max_branches, mode): the config-4 tree, small trees, trees whose
@@ -374,6 +378,47 @@ def make_paged_kv_write(torch, mtp_engine):
                     f"{name}_page_table": kv.page_table.numpy(), f"{name}_k_new": f32(k_new),
                     f"{name}_v_new": f32(v_new), f"{name}_start": np.array([start], np.int64)})
     save("paged_kv_write.npz", **out)
+
+
+# the reference's public functions on the hot path (and around it) whose
+# signatures the drop-in must keep: module -> names ("Class.method" for
+# methods)
+API = {
+    "mtp_kernels": ["fused_rmsnorm_linear", "fused_rmsnorm_linear_fp8", "fused_tree_attention",
+                    "fused_paged_attention", "fused_tree_attn_rmsnorm_linear", "fused_causal_attention",
+                    "fused_causal_attention_fp8", "fused_int4_matmul", "pack_scales", "unpack_scale_tensor",
+                    "quantize_fp8_e4m3", "dequantize_fp8", "quantize_int4", "dequantize_int4",
+                    "build_tuning_config", "KernelTuningConfig.__init__"],
+    "mtp_fused_verify": ["fused_verify", "fused_multi_verify"],
+    "mtp_parallel": ["ParallelPrimitives.__init__", "get_parallel_primitives", "RowParallelLinear.__init__",
+                     "RowParallelLinear.forward", "ColumnParallelLinear.__init__", "ColumnParallelLinear.forward"],
+}
+
+
+def make_api_signatures():
+    """The parameters (name, kind, default) of every function in API, read
+    from the reference's own modules with inspect, as the drop-in contract
+    that tests/test_dropin_api.py checks the modules here against."""
+    import importlib
+    import inspect
+    import json
+    out = {}
+    for mod_name, names in API.items():
+        mod = importlib.import_module(mod_name)
+        for name in names:
+            obj = mod
+            for part in name.split("."):
+                obj = getattr(obj, part)
+            params = []
+            for p_ in inspect.signature(obj).parameters.values():
+                default = None if p_.default is inspect.Parameter.empty else repr(p_.default)
+                params.append([p_.name, p_.kind.name, default])
+            out[f"{mod_name}.{name}"] = params
+    path = os.path.join(HERE, "reference_api.json")
+    with open(path, "w") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+        f.write("\n")
+    print(f"wrote reference_api.json: {len(out)} signatures")
 
 
 # token counts passed to PagedKVCache.reserve, then the logical columns swapped
