@@ -928,8 +928,8 @@ def run_sweep(args):
             ct = cpu_time(lambda: O.rmsnorm_linear(xs, ws * gs[None, :], None, C2["eps"], 1.0))
             for v, t in times:
                 emit(f"config2_M{M}", M, "rows/s", t, "tensor" if tensor else "hbm",
-                     flop / t / 1e12 if tensor else byts / t / 1e9, peaks["bf16_sus"] if tensor else peaks["hbm"],
-                     "measured bf16_tflops_sustained" if tensor else "measured hbm_gbs", rows, ct,
+                     flop / t / 1e12 if tensor else byts / t / 1e9, peaks["bf16"] if tensor else peaks["hbm"],
+                     "measured bf16_tflops (burst)" if tensor else "measured hbm_gbs", rows, ct,
                      {"gemm_schedule": v})
             del x, W
 
@@ -950,10 +950,20 @@ def run_sweep(args):
         wd = O.e4m3_bits_to_f32(wq.view(torch.uint8).cpu().numpy())
         sws = f32(sw)
         ct = cpu_time(lambda: O.rmsnorm_linear_fp8(xd, wd, sws, None, 1e-6))
+        # the FP8 peak, measured here: cuBLASLt's E4M3 GEMM at 8192^3 (no FP8
+        # figure is in the pool's measured peaks)
+        a8 = torch.randn(8192, 8192, generator=g, device=dev).to(torch.float8_e4m3fn)
+        b8 = torch.randn(8192, 8192, generator=g, device=dev).to(torch.float8_e4m3fn)
+        one_a, one_b = torch.ones((8192, 1), device=dev), torch.ones((1, 8192), device=dev)
+        t8 = time_call(lambda: torch._scaled_mm(a8, b8.T, scale_a=one_a, scale_b=one_b, out_dtype=torch.bfloat16),
+                       iters)
+        fp8_peak = 2.0 * 8192 ** 3 / t8 / 1e12
+        del a8, b8
         for v, t in times:
-            emit("config3_fp8", M, "rows/s", t, "tensor", flop / t / 1e12, 2 * peaks["bf16_sus"],
-                 "2 x measured bf16_tflops_sustained (nominal fp8:bf16 ratio; fp8 not measured)", rows, ct,
-                 {"dtype": "e4m3", "gemm_schedule": v})
+            emit("config3_fp8", M, "rows/s", t, "tensor", flop / t / 1e12, fp8_peak,
+                 "cuBLASLt E4M3 GEMM 8192^3 measured in this run (torch._scaled_mm)", rows, ct,
+                 {"dtype": "e4m3", "gemm_schedule": v,
+                  "frac_of_2x_bf16_burst": flop / t / 1e12 / (2 * peaks["bf16"])})
         del x, xq, wq
 
     def sec_config4():
@@ -993,8 +1003,8 @@ def run_sweep(args):
         hs, lms, ds = f32(hid[:2]), f32(lm), dr[:2].cpu().numpy()
         ct = cpu_time(lambda: O.fused_multi_verify(hs, lms, None, ds))
         for v, t in times:
-            emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16_sus"],
-                 "measured bf16_tflops_sustained", 2 * S, ct, {"gemm_schedule": v})
+            emit("config5_verify", Bv * S, "verified candidates/s", t, "tensor", C5_FLOP / t / 1e12, peaks["bf16"],
+                 "measured bf16_tflops (burst)", 2 * S, ct, {"gemm_schedule": v})
         del lm
 
     def sec_ref_bench_fusion_verify():

@@ -152,27 +152,31 @@ __device__ __forceinline__ void token_rows(const Params& p, int b, int kvh, int 
   }
 }
 
-// Fills one 32 KB K or V buffer (128 keys x D = 128, two 16 KB halves of
-// 64 dims, rows 128 bytes, 128-byte swizzle: 16-byte piece j of row r sits
-// at piece j ^ (r & 7)) from the pool rows of token_rows.  Per step the warp
-// moves two tokens (lane l: piece l & 15 of token 2k + (l >> 4)), 16 loads
-// in flight per lane.
+// 16-byte asynchronous copy global -> shared (L2 only); bytes past
+// src_bytes (0 or 16) are zero-filled, so src is not read when it is 0.
+__device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Starts the fill of one 32 KB K or V buffer (128 keys x D = 128, two 16 KB
+// halves of 64 dims, rows 128 bytes, 128-byte swizzle: 16-byte piece j of
+// row r sits at piece j ^ (r & 7)) from the pool rows of token_rows: lane l
+// copies piece l & 15 of tokens 2k + (l >> 4), all 64 of its copies in
+// flight at once; rows of -1 are zero-filled.  The caller waits for them
+// (cp_async_wait_all) before handing the buffer to the tensor cores.
 __device__ __forceinline__ void fill_tokens(uint8_t* dst, const uint8_t* pool, const int (&rows)[4], int lane) {
   const int j = lane & 15, half = j >> 3, jj = j & 7;
+  const uint32_t base = smem_u32(dst) + half * kHalfBytes;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {  // tokens 32 q .. 32 q + 31, whose rows lane (i & 31) holds in rows[q]
-    uint4 v[16];
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
       const int i = 32 * q + 2 * u + (lane >> 4);
       const int row = __shfl_sync(0xffffffffu, rows[q], i & 31);
-      v[u] = row >= 0 ? __ldg(reinterpret_cast<const uint4*>(pool + (int64_t)row * (kD * 2)) + j)
-                      : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int i = 32 * q + 2 * u + (lane >> 4);
-      *reinterpret_cast<uint4*>(dst + half * kHalfBytes + i * 128 + ((jj ^ (i & 7)) << 4)) = v[u];
+      const uint8_t* src = row >= 0 ? pool + (int64_t)row * (kD * 2) + j * 16 : pool;
+      cp_async16(base + i * 128 + ((jj ^ (i & 7)) << 4), src, row >= 0 ? 16u : 0u);
     }
   }
 }
@@ -289,12 +293,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         uint8_t* dst = sBuf + buf * kTileBytes;
         if (per_token) {
-          // generic-proxy stores, made visible to the tensor cores (async
-          // proxy) by each lane's fence before the arrival
+          // K's copies stay in flight while V's are issued; then each lane
+          // waits for its own, fences them for the tensor cores (async
+          // proxy), and both buffers are handed over
           fill_tokens(dst, kv ? p.v_pool : p.k_pool, rows, lane);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&buf_full[buf]);
+          if (kv == 1) {
+            cp_async_wait_all();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(&buf_full[(item - 1) % kNumBuf]);
+              mbar_arrive(&buf_full[buf]);
+            }
+          }
         } else if (is_ctx) {
           if (lane < ppc) {
             const CUtensorMap* map = kv ? &tmV : &tmK;
@@ -310,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    cp_async_wait_all();  // after an abort too: none of this warp's copies may still be landing at exit
   } else if (n_iter > 0 && warp == 10) {
     // ---------------------------------------------------------------- page-table warp
     // Reads the page ids of up to kIdRing context chunks ahead of the TMA

@@ -94,7 +94,7 @@ def _verify_inputs(B, S, K, V, seed):
 
 def test_multi_verify_schedules_agree_and_workspace_rests(N):
     import mtp_fused_verify as mv
-    B, S, K, V = 64, 6, 4096, 128256  # config 5 sizes: 1503 tiles, stream-K on 148 SMs
+    B, S, K, V = 64, 6, 4096, 16032  # one rank of an 8-way verify: 189 tiles, stream-K on 148 SMs
     hid, w, draft = _verify_inputs(B, S, K, V, seed=11)
     before = N.gemm_schedule()
     try:
