@@ -93,7 +93,14 @@ int mtp_device_status(void* stream, int* code_out, int clear);
  * not bit-identical to schedule 0).  Schedule 1 applies only to calls whose
  * workspace has room for it (mtp_gemm_streamk_bytes) and where it is
  * estimated to be faster; other calls run schedule 0.  Returns MTP_ERR_ARG
- * for other modes. */
+ * for other modes.
+ *
+ * Under schedule 0 the verify calls with 16-bit operands and at most 512
+ * logit rows (B*S) run the vocabulary-tiled kernel: pairs of CTAs (thread-
+ * block clusters of 2) each take 256 vocabulary rows against every logit
+ * row, so the weight streams from HBM exactly once; the environment
+ * variable MTP_VERIFY_VT=0 selects the row-tiled kernel instead.  Both give
+ * identical outputs. */
 int mtp_set_gemm_schedule(int mode);
 int mtp_gemm_schedule(void);
 

@@ -21,6 +21,7 @@
 #include "mtp_gemm_simt.cuh"
 #include "mtp_gemm_sk.cuh"
 #include "mtp_gemm_tc.cuh"
+#include "mtp_gemm_vt.cuh"
 #include "mtp_rownorm.cuh"
 #include "mtp_rowattn.cuh"
 #include "mtp_kvwrite.cuh"
@@ -191,6 +192,77 @@ int launch_tc_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, in
   }
 }
 
+// ---------------------------------------------------------------- vocabulary-tiled verify GEMM
+template <int G, int WST, int XST, int FMT>
+int launch_vt_inst(const CUtensorMap& tw, const CUtensorMap& tx, int M, int N, int num_kb, const GemmEpilogue& ep,
+                   cudaStream_t s) {
+  auto kern = vt::gemm_vt_kernel<G, WST, XST, FMT>;
+  constexpr int smem = vt::Cfg<G, WST, XST>::SMEM_BYTES;
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  static int pairs_max[kMaxDevices] = {0};  // clusters resident at once
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(vt::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!pairs_max[dev]) {
+    MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int u = sm_count(dev) / 2;
+    cfg.gridDim = dim3(2 * u, 1, 1);
+    int clusters = 0;
+    MTP_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    if (clusters < 1) return fail(MTP_ERR_CUDA, "no 2-CTA cluster fits the vocabulary-tiled verify kernel");
+    pairs_max[dev] = clusters < u ? clusters : u;
+  }
+  const int tiles = (N + vt::kTileRows - 1) / vt::kTileRows;
+  const int pairs = tiles < pairs_max[dev] ? tiles : pairs_max[dev];
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  MTP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, M, N, num_kb, ep));
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+template <int FMT>
+int launch_vt_groups(int groups, const CUtensorMap& tw, const CUtensorMap& tx, int M, int N, int num_kb,
+                     const GemmEpilogue& ep, cudaStream_t s) {
+  switch (groups) {
+    case 1: return launch_vt_inst<1, 8, 8, FMT>(tw, tx, M, N, num_kb, ep, s);
+    case 2: return launch_vt_inst<2, 6, 6, FMT>(tw, tx, M, N, num_kb, ep, s);
+    case 3: return launch_vt_inst<3, 5, 5, FMT>(tw, tx, M, N, num_kb, ep, s);
+    default: return launch_vt_inst<4, 4, 4, FMT>(tw, tx, M, N, num_kb, ep, s);
+  }
+}
+
+// 16-bit argmax GEMMs of at most 512 candidate rows run the vocabulary-
+// tiled CTA-pair kernel unless MTP_VERIFY_VT=0 is set (then the row-tiled
+// one, for comparisons).  Measured on B200: verify B=64 S=6 V=128256
+// 312 us against 334; one rank of an 8-way verify (V=16032) 59 us against
+// 71; B=40 S=5 with a bias 226 us against 316.
+static bool vt_enabled() {
+  const char* e = getenv("MTP_VERIFY_VT");
+  return !(e && e[0] == '0' && e[1] == 0);
+}
+
+// The verify argmax with weight rows as the MMA's rows (CTA pairs): 16-bit
+// operands, at most 512 candidate rows.
+int launch_gemm_vt(const void* X, const void* W, int ab_dtype, int64_t M, int64_t N, int64_t K,
+                   const GemmEpilogue& ep, cudaStream_t s) {
+  CUtensorMap tw, tx;
+  if (int st = make_kmajor_map(&tw, W, false, ab_dtype, N, K, vt::kRows)) return st;
+  if (int st = make_kmajor_map(&tx, X, false, ab_dtype, M, K, vt::kHalfRows)) return st;
+  const int num_kb = (int)((K * 2 + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  const int groups = (int)((M + vt::kGroupCols - 1) / vt::kGroupCols);
+  if (ab_dtype == MTP_DTYPE_BF16) return launch_vt_groups<1>(groups, tw, tx, (int)M, (int)N, num_kb, ep, s);
+  return launch_vt_groups<0>(groups, tw, tx, (int)M, (int)N, num_kb, ep, s);
+}
+
 // ---------------------------------------------------------------- stream-K
 // Process-wide GEMM schedule: 0 = data-parallel tiles (default), 1 = the
 // stream-K schedule wherever its plan is cheaper and the caller's workspace
@@ -346,6 +418,9 @@ int launch_gemm_tc(const void* A, const void* B, int ab_dtype, bool fp8, int64_t
     if (int st = try_launch_sk(A, B, ab_dtype, fp8, M, N, K, ep, s, sk_ws, sk_bytes, sk_grid, &launched)) return st;
     if (launched) return MTP_OK;
   }
+  if (ep.mode == EPI_ARGMAX && ep.finalize != FIN_CHAIN_PEERS && !fp8 && M >= 1 && M <= vt::kMaxCands &&
+      vt_enabled())
+    return launch_gemm_vt(A, B, ab_dtype, M, N, K, ep, s);
   int dev;
   if (int st = current_device(&dev)) return st;
   const int bn = pick_bn(M, N, sm_count(dev));
