@@ -22,6 +22,7 @@
 #include "mtp_gemm_sk.cuh"
 #include "mtp_gemm_tc.cuh"
 #include "mtp_gemm_vt.cuh"
+#include "mtp_gemm_pair.cuh"
 #include "mtp_rownorm.cuh"
 #include "mtp_rowattn.cuh"
 #include "mtp_kvwrite.cuh"
@@ -263,6 +264,116 @@ int launch_gemm_vt(const void* X, const void* W, int ab_dtype, int64_t M, int64_
   return launch_vt_groups<0>(groups, tw, tx, (int)M, (int)N, num_kb, ep, s);
 }
 
+// ---------------------------------------------------------------- CTA-pair store GEMM
+// Clusters of 2 resident at once for a pair kernel (1 CTA per SM).
+template <typename Kern>
+int pair_clusters(Kern kern, int smem, int threads, int dev, int* out) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int u = sm_count(dev) / 2;
+  cfg.gridDim = dim3(2 * u, 1, 1);
+  int clusters = 0;
+  MTP_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+  if (clusters < 1) return fail(MTP_ERR_CUDA, "no 2-CTA cluster fits the pair GEMM");
+  *out = clusters < u ? clusters : u;
+  return MTP_OK;
+}
+
+template <int BN, bool FP8, int FMT>
+int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int num_kb, const GemmEpilogue& ep,
+                     cudaStream_t s) {
+  auto kern = pg::gemm_pair_kernel<BN, FP8, FMT>;
+  constexpr int smem = pg::Cfg<BN>::SMEM_BYTES;
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  static int pairs_max[kMaxDevices] = {0};
+  if (!pairs_max[dev]) {
+    MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (int st = pair_clusters(kern, smem, pg::kThreads, dev, &pairs_max[dev])) return st;
+  }
+  const int tiles = ((M + pg::kTileM - 1) / pg::kTileM) * ((N + BN - 1) / BN);
+  const int pairs = tiles < pairs_max[dev] ? tiles : pairs_max[dev];
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(pg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MTP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, num_kb, ep));
+  MTP_LAUNCH_CHECK();
+  return MTP_OK;
+}
+
+// Tile width of the pair GEMM: fewest rounds x BN (the mainloop time of a
+// round is proportional to BN), the widest on a tie.
+int pick_bn_pair(int64_t M, int64_t N, int pairs) {
+  static const int cands[5] = {256, 224, 192, 160, 128};
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int bn : cands) {
+    if (bn > 128 && N <= 128) continue;
+    const int64_t tiles = ((M + pg::kTileM - 1) / pg::kTileM) * ((N + bn - 1) / bn);
+    const int64_t rounds = (tiles + pairs - 1) / pairs;
+    const int64_t cost = rounds * bn;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <bool FP8, int FMT>
+int launch_pair_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int num_kb,
+                   const GemmEpilogue& ep, cudaStream_t s) {
+  switch (bn) {
+    case 256: return launch_pair_inst<256, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    case 224: return launch_pair_inst<224, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    case 192: return launch_pair_inst<192, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    case 160: return launch_pair_inst<160, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+    default: return launch_pair_inst<128, FP8, FMT>(ta, tb, M, N, num_kb, ep, s);
+  }
+}
+
+// Store-epilogue GEMMs of 129-4096 rows run on CTA pairs unless
+// MTP_GEMM_PAIR=0 is set (then the one-CTA kernel, for comparisons).
+// Measured on B200 (RMSNorm-linear, N=14336, K=4096): M=512 and 2048 5-8 %
+// faster on pairs, FP8 M=1024 N=28672 K=8192 7 %; M=8192 12 % slower (its
+// operands no longer fit L2 and the pair tiles' order re-reads them more).
+static bool pair_enabled() {
+  const char* e = getenv("MTP_GEMM_PAIR");
+  return !(e && e[0] == '0' && e[1] == 0);
+}
+
+int launch_gemm_pair(const void* A, const void* B, int ab_dtype, bool fp8, int64_t M, int64_t N, int64_t K,
+                     const GemmEpilogue& ep, cudaStream_t s) {
+  int dev;
+  if (int st = current_device(&dev)) return st;
+  const int bn = pick_bn_pair(M, N, sm_count(dev) / 2);
+  CUtensorMap ta, tb;
+  if (int st = make_kmajor_map(&ta, A, fp8, ab_dtype, M, K, pg::kRows)) return st;
+  if (int st = make_kmajor_map(&tb, B, fp8, ab_dtype, N, K, bn / 2)) return st;
+  const int eb = fp8 ? 1 : 2;
+  const int num_kb = (int)((K * eb + tc::kKBlockBytes - 1) / tc::kKBlockBytes);
+  if (fp8) return launch_pair_bn<true, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
+  if (ab_dtype == MTP_DTYPE_BF16) return launch_pair_bn<false, 1>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
+  return launch_pair_bn<false, 0>(bn, ta, tb, (int)M, (int)N, num_kb, ep, s);
+}
+
 // ---------------------------------------------------------------- stream-K
 // Process-wide GEMM schedule: 0 = data-parallel tiles (default), 1 = the
 // stream-K schedule wherever its plan is cheaper and the caller's workspace
@@ -421,6 +532,8 @@ int launch_gemm_tc(const void* A, const void* B, int ab_dtype, bool fp8, int64_t
   if (ep.mode == EPI_ARGMAX && ep.finalize != FIN_CHAIN_PEERS && !fp8 && M >= 1 && M <= vt::kMaxCands &&
       vt_enabled())
     return launch_gemm_vt(A, B, ab_dtype, M, N, K, ep, s);
+  if (ep.mode == EPI_STORE && M > tc::kBM && M <= 4096 && pair_enabled())
+    return launch_gemm_pair(A, B, ab_dtype, fp8, M, N, K, ep, s);
   int dev;
   if (int st = current_device(&dev)) return st;
   const int bn = pick_bn(M, N, sm_count(dev));
