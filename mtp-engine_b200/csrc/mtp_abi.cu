@@ -1287,6 +1287,7 @@ struct TreePlan {
   size_t ws_bytes = 256;
 };
 
+
 TreePlan tree_plan(int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t ctx_len, int64_t page_size,
                    int64_t num_pages, int dtype) {
   constexpr int chunk = attn::kChunk;

@@ -213,7 +213,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+      if (lane == 0) {  // the accumulator is read (tcgen05 wait and fence above)
+        if (leader) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
+      }
     }
   }
 

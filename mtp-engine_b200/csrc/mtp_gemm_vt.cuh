@@ -313,7 +313,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         // the group is in registers: free it (the leader's barrier counts both CTAs)
-        if (lane == 0) mbar_arrive_cluster(cluster_addr(&gempty[s & 3], 0));
+        if (lane == 0) {
+          if (leader) mbar_arrive(&gempty[s & 3]);
+          else mbar_arrive_remote(cluster_addr(&gempty[s & 3], 0));
+        }
         if (!__any_sync(0xffffffffu, v_ok)) continue;  // the whole quadrant is past the vocabulary
 #pragma unroll
         for (int c = 0; c < 4; ++c) {

@@ -71,8 +71,12 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* des
       "l"(reinterpret_cast<uint64_t>(desc)), "r"(c0), "r"(c1), "r"(bar_cluster)
       : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+// arrive on a barrier of either CTA of the pair (cluster address) with the
+// default, CTA-scoped release: for hand-offs of tensor-memory data, whose
+// ordering tcgen05.wait / tcgen05.fence::before_thread_sync provide (a
+// cluster-scoped release costs hundreds of cycles per arrival)
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
