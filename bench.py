@@ -254,7 +254,15 @@ def run_ours(args):
     N.set_gemm_schedule(1 if args.gemm_schedule == "streamk" else 0)  # before any workspace exists
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+        opts = None
+        if args.nccl_max_ctas > 0:
+            # NCCL's kernels run beside this rank's own (the candidates'
+            # all-gather beside stages 1-2): cap their CTAs so they fit in the
+            # SMs those stages leave free instead of delaying their CTAs
+            # (uncapped, the all-gather cost the stage beside it ~30 us)
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.config.max_ctas = args.nccl_max_ctas
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev, pg_options=opts)
     prim = mp.get_parallel_primitives()
     assert C2["N"] % world == 0 and C4["Hkv"] % world == 0
     # strong: the 1-GPU job split tensor-parallel (columns / KV heads / vocabulary).
@@ -403,7 +411,10 @@ def run_ours(args):
             e = ev[i]
             e[0].record(stream)
             if weak:
-                gather(hidden, draft)  # overlaps stages 1 and 2
+                # overlaps stages 1 and 2: NCCL's kernel (capped at
+                # --nccl-max-ctas CTAs) runs in the SMs the pair GEMM leaves
+                # free (128 tiles take 64 pairs, 128 of the 148 SMs)
+                gather(hidden, draft)
             run[0]()
             e[1].record(stream)
             run[1]()
@@ -1231,6 +1242,8 @@ def main():
     ap.add_argument("--graph", action="store_true", help="also replay captured graphs when n_gpus > 1")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--sweep", action="store_true", help="time every benchmark config on its own (1 GPU)")
+    ap.add_argument("--nccl-max-ctas", type=int, default=8,
+                    help="N > 1: cap on the CTAs of NCCL's kernels (0: NCCL's own choice)")
     ap.add_argument("--exchange", choices=["nccl", "p2p", "fused", "abi"], default="nccl",
                     help="vocab-parallel key exchange on N > 1: NCCL all-reduce, the peer-memory kernel, "
                          "the all-reduce fused into the shard GEMM, or the one-call C-ABI verify over the "

@@ -299,8 +299,13 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     MTP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     if (int st = pair_clusters(kern, smem, pg::kThreads, dev, &pairs_max[dev])) return st;
   }
+  // As few pairs as finish the tiles in the same number of rounds (128 tiles
+  // on 74 pairs take two rounds; 64 pairs take two as well): the makespan is
+  // unchanged and the SMs left over serve whatever runs beside the GEMM
+  // (the candidates' all-gather of a vocab-parallel verify).
   const int tiles = ((M + pg::kTileM - 1) / pg::kTileM) * ((N + BN - 1) / BN);
-  const int pairs = tiles < pairs_max[dev] ? tiles : pairs_max[dev];
+  const int rounds = (tiles + pairs_max[dev] - 1) / pairs_max[dev];
+  const int pairs = (tiles + rounds - 1) / rounds;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
