@@ -718,6 +718,13 @@ int mtp_attn_trace_read(unsigned long long* host, int n) {
   MTP_CUDA_TRY(cudaMemcpyFromSymbol(host, attn::g_attn_trace, sizeof(unsigned long long) * (n < cap ? n : cap)));
   return MTP_OK;
 }
+// per-CTA phase stamps, 8 per CTA
+int mtp_attn_cta_read(unsigned long long* host, int n) {
+  MTP_CUDA_TRY(cudaDeviceSynchronize());
+  const int cap = (int)(sizeof(attn::g_attn_cta) / sizeof(unsigned long long));
+  MTP_CUDA_TRY(cudaMemcpyFromSymbol(host, attn::g_attn_cta, sizeof(unsigned long long) * (n < cap ? n : cap)));
+  return MTP_OK;
+}
 #endif
 
 int mtp_gemm_test(const void* A, const void* B, int ab_dtype, float* C, int64_t M, int64_t N, int64_t K,

@@ -60,17 +60,34 @@ static_assert(kTileBytes % 1024 == 0 && (kIdRing * kMaxPagesPerChunk * 4) % 8 ==
 static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 // Optional cycle stamps of CTA 0 (build with -DMTP_ATTN_TRACE): slot
-// (role, tile, iteration) -> clock64.  Compiled out otherwise.
+// (kind, tile, iteration) -> clock64.  Compiled out otherwise.  Kinds:
+// softmax 0 scores ready, 1 scores loaded, 8 row max done, 2 previous PV
+// seen done, 9 first half of P handed over, 3 both halves handed over;
+// MMA warp 10 first half of P seen, 4 second half seen, 11 PV committed,
+// 5 next S issued; producer 6 K buffer acquired, 7 V buffer acquired.
+// The same builds also stamp every CTA's phases (CTA_STAMP slot k of CTA
+// blockIdx.x; slot 0 is the entry %globaltimer, the others clock64):
+// 1 entry, 2 Q and first K landed (MMA warp), 3 first scores seen, 4 last
+// context chunk's P stored, 5 last chunk's P stored, 6 output written, 7 exit
+// (softmax tile 0, row 0, for 3-6).
 #ifdef MTP_ATTN_TRACE
-static __device__ unsigned long long g_attn_trace[8 * 2 * 64];
+static __device__ unsigned long long g_attn_trace[12 * 2 * 64];
+static __device__ unsigned long long g_attn_cta[1024 * 8];
 #define ATTN_TRACE_IF(cond, k, tile, it)                                         \
   do {                                                                           \
     if (blockIdx.x == 0 && (cond) && (it) < 64)                                  \
       g_attn_trace[(((k) * 2 + (tile)) * 64 + (it))] = clock64();                \
   } while (0)
+#define CTA_STAMP(cond, k)                                                       \
+  do {                                                                           \
+    if ((cond) && blockIdx.x < 1024) g_attn_cta[blockIdx.x * 8 + (k)] = clock64(); \
+  } while (0)
 #else
 #define ATTN_TRACE_IF(cond, k, tile, it) \
   do {                                   \
+  } while (0)
+#define CTA_STAMP(cond, k) \
+  do {                     \
   } while (0)
 #endif
 #define ATTN_TRACE(k, tile, it) ATTN_TRACE_IF(r == 0, k, tile, it)
@@ -131,6 +148,22 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi, int dtype) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// P for keys 64h .. 64h + 63 of a score row: 2^(s*mul - m) packed as 16-bit
+// pairs into s[32h .. 32h + 31] (s[j] is free once s[2j], s[2j+1] are read),
+// with the running sums in (ls0, ls1).
+template <int AB_FMT>
+__device__ __forceinline__ void exp_pack_half(uint32_t (&s)[128], int h, float mul, float m_use, float& ls0,
+                                              float& ls1) {
+#pragma unroll
+  for (int j = 32 * h; j < 32 * h + 32; ++j) {
+    float x0, x1;
+    ffma2(x0, x1, __uint_as_float(s[2 * j]), __uint_as_float(s[2 * j + 1]), mul, mul, -m_use, -m_use);
+    const float e0 = ex2(x0), e1 = ex2(x1);
+    add2(ls0, ls1, e0, e1);
+    s[j] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
+  }
+}
+
 // Per-token gather of a context chunk (tables that are not page-granular).
 // rows[i] (lane l) = pool row -- ((page * B + b) * Hkv + h) * page_size + slot,
 // 256 bytes of K or V -- of token tok0 + l + 32 i, or -1 past the context or
@@ -181,6 +214,21 @@ __device__ __forceinline__ void fill_tokens(uint8_t* dst, const uint8_t* pool, c
   }
 }
 
+// Keep-bits of tree keys m0 .. m0 + 31 for the query row of tree node
+// t_node (bit k set: tree_mask[t_node, m0 + k] > 0.5); 0 past T or for a
+// padding row.
+__device__ __forceinline__ uint32_t tree_mask_bits(const Params& p, bool row_ok, int t_node, int m0) {
+  uint32_t bits = 0;
+  if (row_ok && m0 < p.T) {
+    const float* mrow = p.tree_mask + (int64_t)t_node * p.T + m0;
+    const int n = min(32, p.T - m0);
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k)
+      if (k < n && __ldg(mrow + k) > 0.5f) bits |= 1u << k;
+  }
+  return bits;
+}
+
 // AB_FMT: 1 = bf16, 0 = f16 (q/k/v dtype)
 template <int AB_FMT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -214,6 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int c0 = split * p.chunks_per_split;
   const int c1 = min(p.n_chunks, c0 + p.chunks_per_split);
   const int n_iter = c1 - c0;
+#ifdef MTP_ATTN_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_attn_cta[blockIdx.x * 8] = globaltimer_ns();
+#endif
+  CTA_STAMP(threadIdx.x == 0, 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -397,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       (acc || k > 0) ? 1u : 0u);
       };
       if (ok && (ok = wait_item(0))) {
+        CTA_STAMP(true, 2);
         tc_fence_after();
         for (int t = 0; t < p.n_tiles; ++t) {
           issue_s(t, 0);
@@ -413,13 +466,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(ok = wait_item(vitem))) break;
             tc_fence_after();
           }
+          ATTN_TRACE_IF(true, 10, t, i);
           issue_pv(t, vitem % kNumBuf, 0, i > 0);  // first 64 keys while the softmax finishes the rest
           if (!(ok = mbar_wait(&p_full[2 * t + 1], i & 1, abort_flag))) break;
           tc_fence_after();
           ATTN_TRACE_IF(true, 4, t, i);
           issue_pv(t, vitem % kNumBuf, 1, true);
           umma_commit(&pv_done[t]);
-          ATTN_TRACE_IF(true, 2, t, 32 + (i & 31));
+          ATTN_TRACE_IF(true, 11, t, i);
           if (t == p.n_tiles - 1) umma_commit(&buf_empty[vitem % kNumBuf]);
           if (i + 1 < n_iter) {
             if (t == 0) {
@@ -450,6 +504,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t o_addr = tmem_base + lane_off + (uint32_t)(256 + t * 128);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    // Keep-bits of this row over the first 128 tree keys, read from the
+    // float mask before the first scores arrive: the loads overlap the
+    // pipeline fill, and the tree chunk's softmax makes no global loads
+    // (a second tree chunk, T > 128, reads its bits when it comes).
+    uint32_t tbits[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) tbits[w] = tree_mask_bits(p, row_ok, t_node, 32 * w);
     for (int i = 0; i < n_iter; ++i) {
       const int c = c0 + i;
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], i & 1, abort_flag))) {
@@ -458,6 +519,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       ATTN_TRACE(0, t, i);
+      CTA_STAMP(t == 0 && r == 0 && i == 0, 3);
+      // keep-bits of the 128 keys of this chunk (bit k of word w: key 32w + k)
+      uint32_t mw[4];
+      if (c < p.n_ctx_chunks) {
+        const int valid = p.ctx_len - c * kChunk;  // keys [0, valid) are context tokens
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int v = valid - 32 * w;
+          mw[w] = v >= 32 ? 0xffffffffu : (v <= 0 ? 0u : ((1u << v) - 1u));
+        }
+      } else {
+        const int m0 = (c - p.n_ctx_chunks) * kChunk;
+        if (m0 == 0) {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) mw[w] = tbits[w];
+        } else {
+#pragma unroll 1
+          for (int w = 0; w < 4; ++w) mw[w] = tree_mask_bits(p, row_ok, t_node, m0 + 32 * w);
+        }
+      }
+      const bool no_masked = (mw[0] & mw[1] & mw[2] & mw[3]) == 0xffffffffu;
       // the whole 128-column score row in one TMEM round trip
       uint32_t s[128];
 #pragma unroll
@@ -468,29 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // host), so max(s)*scale == max(s*scale) and the scale is folded into
       // the exponent below.  Masked keys become -inf.  Eight independent
       // partial maxima keep the dependency chains short.
-      uint32_t mw[4];  // keep-bits of the 128 keys of this chunk
-      if (c < p.n_ctx_chunks) {
-        const int valid = p.ctx_len - c * kChunk;  // keys [0, valid) are context tokens
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const int v = valid - 32 * w;
-          mw[w] = v >= 32 ? 0xffffffffu : (v <= 0 ? 0u : ((1u << v) - 1u));
-        }
-      } else {
-        const int m0 = (c - p.n_ctx_chunks) * kChunk;
-        const float* mrow = p.tree_mask + (int64_t)(row_ok ? t_node : 0) * p.T;
-#pragma unroll 1
-        for (int w = 0; w < 4; ++w) {
-          uint32_t bits = 0;
-#pragma unroll 8
-          for (int k = 0; k < 32; ++k) {
-            const int m = m0 + 32 * w + k;
-            if (row_ok && m < p.T && __ldg(mrow + m) > 0.5f) bits |= 1u << k;
-          }
-          mw[w] = bits;
-        }
-      }
-      if ((mw[0] & mw[1] & mw[2] & mw[3]) != 0xffffffffu) {
+      if (!no_masked) {
 #pragma unroll
         for (int j = 0; j < 128; ++j)
           if (!((mw[j >> 5] >> (j & 31)) & 1u)) s[j] = 0xff800000u;  // -inf
@@ -506,6 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                             fmaxf(m8[6], m8[7]));
       const float mul = p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
+      ATTN_TRACE(8, t, i);
       if (i > 0) {
         // P and O may be touched only after the previous PV completed
         if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[t], (i - 1) & 1, abort_flag))) {
@@ -542,22 +603,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-#pragma unroll
-        for (int j = 32 * h; j < 32 * h + 32; ++j) {
-          float x0, x1;
-          ffma2(x0, x1, __uint_as_float(s[2 * j]), __uint_as_float(s[2 * j + 1]), mul, mul, -m_use, -m_use);
-          const float e0 = ex2(x0), e1 = ex2(x1);
-          add2(ls0, ls1, e0, e1);
-          s[j] = pack_bf16(e0, e1, AB_FMT == 1 ? MTP_DTYPE_BF16 : MTP_DTYPE_F16);
-        }
+        exp_pack_half<AB_FMT>(s, h, mul, m_use, ls0, ls1);
         tmem_st32(s_addr + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * h]));
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[2 * t + h]);
+        ATTN_TRACE_IF(r == 0 && h == 0, 9, t, i);
       }
       l_run += ls0 + ls1;
       ATTN_TRACE(3, t, i);
+      CTA_STAMP(t == 0 && r == 0 && c == p.n_ctx_chunks - 1, 4);
+      CTA_STAMP(t == 0 && r == 0 && i == n_iter - 1, 5);
     }
     if (ok && __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (n_iter - 1) & 1, abort_flag))) {
       tc_fence_after();
@@ -598,6 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.part_ml[slot * 2] = m_run;
         p.part_ml[slot * 2 + 1] = l_run;
       }
+      CTA_STAMP(t == 0 && r == 0, 6);
     }
   }
 
@@ -607,6 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
+  CTA_STAMP(threadIdx.x == 0, 7);
 }
 
 // Merge split partials: out = sum_s w_s O_s / sum_s w_s l_s, w_s = 2^(m_s - max m).
