@@ -1432,6 +1432,21 @@ int launch_tree_attention_tc(const TreePlan& pl, const void* q, const void* k_pa
   if (int st = current_device(&dev)) return st;
   const int grid = (int)(B * Hkv * pl.splits);
   static bool attr[2][kMaxDevices] = {};
+  // setmaxnreg moves registers between warpgroups inside the launch's
+  // reservation; with a different reservation an increase could wait forever
+  static bool regs_ok[2][kMaxDevices] = {};
+  {
+    const int di = dtype == MTP_DTYPE_BF16 ? 0 : 1;
+    if (!regs_ok[di][dev]) {
+      cudaFuncAttributes fa;
+      MTP_CUDA_TRY(dtype == MTP_DTYPE_BF16 ? cudaFuncGetAttributes(&fa, attn::tree_attention_tc_kernel<1>)
+                                           : cudaFuncGetAttributes(&fa, attn::tree_attention_tc_kernel<0>));
+      if (fa.numRegs != attn::kLaunchRegs)
+        return fail(MTP_ERR_CUDA, "tree attention kernel reserves %d registers per thread, its register split "
+                    "needs %d", fa.numRegs, attn::kLaunchRegs);
+      regs_ok[di][dev] = true;
+    }
+  }
   if (dtype == MTP_DTYPE_BF16) {
     if (int st = set_smem_once(attn::tree_attention_tc_kernel<1>, attn::kSmemBytes, attr[0], dev)) return st;
     attn::tree_attention_tc_kernel<1><<<grid, attn::kThreads, attn::kSmemBytes, s>>>(tq, tk, tv, ttk, ttv, p);

@@ -8,30 +8,33 @@
 // held as two 128-row tiles (row r = t_local*G + g) for the whole kernel, so
 // each K/V byte is read from HBM once per unit and feeds 256 query rows.
 //
-// 352 threads, one CTA per SM:
-//   warp 0      TMA producer: Q once (4-D map over [B,T,Hq,D]); then per
+// 384 threads, one CTA per SM, roles grouped by warpgroup:
+//   warps 0-3   softmax for query tile 0, warps 4-7 for tile 1 (warpgroups
+//               0 and 1, 224 registers per thread after set-up): one query
+//               row per thread; tcgen05.ld of the scores, mask (context
+//               length, or the tree ancestor mask), running max in the log2
+//               domain with lazy rescaling (O in TMEM is rescaled only when
+//               the max grows by more than 2^8), exp2, P packed to bf16
+//               pairs and stored back into TMEM with tcgen05.st.
+//   warp 8      TMA producer: Q once (4-D map over [B,T,Hq,D]); then per
 //               128-key chunk the K and V slabs -- context chunks gather
 //               128/page_size pages of the PagedKVCache pool
 //               [P,B,Hkv,page_size,D] (each (page,b,h) slab is contiguous),
 //               the tree chunk reads [B,Hkv,T,D] -- into a 5-deep ring of
 //               32 KB buffers, 128-byte swizzled; one lane per page slab.
-//   warp 1      TMEM allocator + tcgen05.mma issuer:
+//   warp 9      TMEM allocator + tcgen05.mma issuer:
 //               S_t = Q_t K^T (M128 N128 K128) and O_t += P_t V
 //               (M128 N128 K128, P read from TMEM, V MN-major from shared
 //               memory), accumulators in TMEM (S0, S1, O0, O1 = 4 x 128
 //               columns; P_t overwrites the first 64 columns of S_t), ordered
 //               S0 S1 | PV0 S0' PV1 S1' | ... so one tile's softmax overlaps
 //               the other tile's MMAs.
-//   warps 2-5   softmax for tile 0, warps 6-9 for tile 1: one query row per
-//               thread; tcgen05.ld of the scores, mask (context length, or
-//               the tree ancestor mask), running max in the log2 domain with
-//               lazy rescaling (O in TMEM is rescaled only when the max
-//               grows by more than 2^8), exp2, P packed to bf16 pairs and
-//               stored back into TMEM with tcgen05.st.
 //   warp 10     page-table reader: stages the page ids of up to 16 chunks
 //               ahead of the TMA producer (shared-memory ring) and marks
 //               chunks whose table is not page-granular, which the producer
 //               then gathers token by token (16-byte loads into the ring).
+//   warp 11     idle (completes warpgroup 2, 56 registers per thread with
+//               warps 8-10).
 // Long contexts with few units are split over CTAs (flash-decoding); the
 // partial (O, max, sum) triples are merged by attn_merge_kernel.
 // Every wait is bounded (mbar_wait).  No clusters; every TMA load fills its own CTA.
@@ -42,7 +45,16 @@
 namespace mtp {
 namespace attn {
 
-constexpr int kThreads = 352;                    // 11 warps (see the role list above)
+// Roles grouped by warpgroup so registers can move between them: softmax
+// tiles 0 / 1 = warpgroups 0 / 1 (warps 0-3, 4-7), producer 8, MMA 9, page
+// table 10, warp 11 idle.  After set-up warpgroup 2 drops to kRegsAux
+// registers per thread and warpgroups 0-1 rise to kRegsSoftmax; per SM
+// sub-partition (one warp of each warpgroup) 2 * 224 + 56 = 3 * 168, the
+// registers the launch reserves (checked on the host before every launch).
+constexpr int kThreads = 384;
+constexpr int kWarpProducer = 8, kWarpMma = 9, kWarpTable = 10, kWarpSoftmax0 = 0;
+constexpr int kLaunchRegs = 168, kRegsSoftmax = 224, kRegsAux = 56;
+static_assert(2 * kRegsSoftmax + kRegsAux == 3 * kLaunchRegs, "register split must equal the launch's reservation");
 constexpr int kD = 128;
 constexpr int kChunk = 128;                      // keys per chunk
 constexpr int kHalfBytes = 128 * 128;            // 128 rows x 128 bytes (64 bf16 of D)
@@ -287,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -296,7 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (n_iter > 0 && warp == 0) {
+  if (warp >= 8) {  // warpgroup 2: producer, MMA, page table, idle
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsAux));
+  if (n_iter > 0 && warp == kWarpProducer) {
     // ---------------------------------------------------------------- TMA producer (whole warp)
     // lane i < pages_per_chunk issues the loads of page slot i of a context
     // chunk; page ids come checked from the table warp through sIds.
@@ -374,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     cp_async_wait_all();  // after an abort too: none of this warp's copies may still be landing at exit
-  } else if (n_iter > 0 && warp == 10) {
+  } else if (n_iter > 0 && warp == kWarpTable) {
     // ---------------------------------------------------------------- page-table warp
     // Reads the page ids of up to kIdRing context chunks ahead of the TMA
     // producer and decides how each chunk is gathered.  The reference
@@ -422,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&ids_full[slot]);
     }
-  } else if (n_iter > 0 && warp == 1) {
+  } else if (n_iter > 0 && warp == kWarpMma) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, abort_flag);
@@ -491,9 +505,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, abort_flag, /*honour_abort=*/false);
     }
-  } else if (n_iter > 0 && warp >= 2 && (warp - 2) / 4 < p.n_tiles) {
+  }
+  } else {  // warpgroups 0-1: softmax of query tiles 0 and 1
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+  if (n_iter > 0 && (warp - kWarpSoftmax0) / 4 < p.n_tiles) {
     // ---------------------------------------------------------------- softmax
-    const int t = (warp - 2) / 4;
+    const int t = (warp - kWarpSoftmax0) / 4;
     const int q = warp & 3;
     const int r = q * 32 + lane;  // row within the tile == TMEM lane
     const int t_node = t * p.t_per_tile + r / p.G;
@@ -658,10 +675,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       CTA_STAMP(t == 0 && r == 0, 6);
     }
   }
+  }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
