@@ -10,7 +10,7 @@
 //
 // 384 threads, one CTA per SM, roles grouped by warpgroup:
 //   warps 0-3   softmax for query tile 0, warps 4-7 for tile 1 (warpgroups
-//               0 and 1, 224 registers per thread after set-up): one query
+//               0 and 1, 184 registers per thread after set-up): one query
 //               row per thread; tcgen05.ld of the scores, mask (context
 //               length, or the tree ancestor mask), running max in the log2
 //               domain with lazy rescaling (O in TMEM is rescaled only when
@@ -33,7 +33,7 @@
 //               ahead of the TMA producer (shared-memory ring) and marks
 //               chunks whose table is not page-granular, which the producer
 //               then gathers token by token (16-byte loads into the ring).
-//   warp 11     idle (completes warpgroup 2, 56 registers per thread with
+//   warp 11     idle (completes warpgroup 2, 136 registers per thread with
 //               warps 8-10).
 // Long contexts with few units are split over CTAs (flash-decoding); the
 // partial (O, max, sum) triples are merged by attn_merge_kernel.
@@ -49,11 +49,15 @@ namespace attn {
 // tiles 0 / 1 = warpgroups 0 / 1 (warps 0-3, 4-7), producer 8, MMA 9, page
 // table 10, warp 11 idle.  After set-up warpgroup 2 drops to kRegsAux
 // registers per thread and warpgroups 0-1 rise to kRegsSoftmax; per SM
-// sub-partition (one warp of each warpgroup) 2 * 224 + 56 = 3 * 168, the
+// sub-partition (one warp of each warpgroup) 2 * 184 + 136 = 3 * 168, the
 // registers the launch reserves (checked on the host before every launch).
+// 136 keeps the producer's per-token gather (64 asynchronous copies per
+// lane in flight) as fast as with 168; at 120 or fewer it ran 30-45 %
+// slower on fully per-token tables, while the softmax gains little above
+// 184 (224: 3 % more on page-granular tables).
 constexpr int kThreads = 384;
 constexpr int kWarpProducer = 8, kWarpMma = 9, kWarpTable = 10, kWarpSoftmax0 = 0;
-constexpr int kLaunchRegs = 168, kRegsSoftmax = 224, kRegsAux = 56;
+constexpr int kLaunchRegs = 168, kRegsSoftmax = 184, kRegsAux = 136;
 static_assert(2 * kRegsSoftmax + kRegsAux == 3 * kLaunchRegs, "register split must equal the launch's reservation");
 constexpr int kD = 128;
 constexpr int kChunk = 128;                      // keys per chunk
